@@ -1,0 +1,460 @@
+"""Benchmark: one full MuonAdamW optimizer step on the Llama-3-8B-shaped parameter set.
+
+    python bench.py [--gpus N --steps K --warmup W] [--config 8b|1b3|c1] [--impl ours|reference]
+
+A step is one ``MuonAdamW.step()`` (AdamW branch + Muon branch with ns_steps
+Newton-Schulz iterations) over the whole synthetic parameter set, already in
+HBM.  ``value`` is the device-timed ms/step (CUDA events, max over ranks);
+``e2e`` repeats the step through the public API with this step's gradients
+copied in from pinned host memory and a small result read back, all inside
+the timed region.  ``roofline`` reports the dominant kernel (the tcgen05
+Newton-Schulz update GEMM) against the measured peaks in MEASURED_PEAKS.json,
+timed live with CUDA events on the launching stream; ``kernels`` has every
+kernel family.  ``cpu_baseline`` times the reference's CPU path
+(``torch.optim`` AdamW(fused) + Muon, the PyTorchMuonAdamW wrapper, restated
+under oracle/) on a bounded sample and extrapolates to the full step.
+
+With ``--impl reference`` only that CPU measurement runs (rank 0), each step a
+bounded sample extrapolated to the full step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "triton-muonadamw_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+import torch.nn as nn  # noqa: E402
+
+COEFFS = (3.4445, -4.7750, 2.0315)
+HBM_FALLBACK, TF_FALLBACK, TF_SUSTAINED_FALLBACK = 6650.0, 1590.0, 1400.0
+
+
+# ----------------------------------------------------------------- configs
+def llama_shapes(d, layers, n_heads, n_kv_heads, ffn, vocab, tied=False):
+    hd = d // n_heads
+    adam = [("embed", (vocab, d))] + ([] if tied else [("head", (vocab, d))])
+    muon = []
+    for i in range(layers):
+        adam += [(f"l{i}.attn_norm", (d,)), (f"l{i}.ffn_norm", (d,))]
+        muon += [(f"l{i}.wq", (n_heads * hd, d)), (f"l{i}.wk", (n_kv_heads * hd, d)),
+                 (f"l{i}.wv", (n_kv_heads * hd, d)), (f"l{i}.wo", (d, n_heads * hd)),
+                 (f"l{i}.gate", (ffn, d)), (f"l{i}.up", (ffn, d)), (f"l{i}.down", (d, ffn))]
+    adam.append(("final_norm", (d,)))
+    return adam, muon
+
+
+CONFIGS = {
+    "8b": dict(name="llama3-8b-shaped", shapes=lambda: llama_shapes(4096, 32, 32, 8, 14336, 128256),
+               adam=dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)),
+    "1b3": dict(name="llama-1.3b", shapes=lambda: llama_shapes(2048, 24, 16, 16, 5504, 32000),
+                adam=dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)),
+}
+
+
+class ShapedParams(nn.Module):
+    """Parameter container with the named shapes; embed/head exposed for the auto split."""
+
+    def __init__(self, adam, muon, device, seed):
+        super().__init__()
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.names = []
+        for name, shape in adam + muon:
+            t = torch.empty(shape, device=device, dtype=torch.float32)
+            t.normal_(0.0, 0.02, generator=gen)
+            self.register_parameter(name.replace(".", "_"), nn.Parameter(t))
+            self.names.append(name.replace(".", "_"))
+        self._embed = nn.Module()
+        self._embed.weight = self.embed
+        self._head = nn.Module() if hasattr(self, "head") else None
+        if self._head is not None:
+            self._head.weight = self.head
+
+    def get_input_embeddings(self):
+        return self._embed
+
+    def get_output_embeddings(self):
+        return self._head
+
+
+# ----------------------------------------------------------------- helpers
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return HBM_FALLBACK, TF_FALLBACK, TF_SUSTAINED_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        load = [s for s in sm if smax and s > 0.5 * max(smax)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class PhaseTimer:
+    """CUDA events around each launch of the step, on the launching (current) stream."""
+
+    def __init__(self):
+        self.events = []
+
+    def mark(self, label):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.events.append((label, e))
+
+    def durations(self):
+        out = {}
+        for (label, a), (_, b) in zip(self.events, self.events[1:]):
+            if label is None:
+                continue
+            out.setdefault(label, []).append(a.elapsed_time(b))
+        return out
+
+
+def ns_flops_sym(shape):
+    m, n = min(shape), max(shape)
+    return {"gram": float(m) * m * n, "poly": float(m) ** 3, "update": 2.0 * m * m * n}
+
+
+# ----------------------------------------------------------------- CPU baseline
+def cpu_sample(cfg_key, adam_cfg, ns_steps):
+    """Time the reference's CPU path on one matrix per distinct Muon shape + an AdamW chunk; extrapolate."""
+    from oracle.muon_adamw_oracle import ReferenceWrapperCPU  # noqa: PLC0415
+    torch.set_num_threads(os.cpu_count() or 1)
+    adam, muon = CONFIGS[cfg_key]["shapes"]()
+    counts = {}
+    for _, s in muon:
+        counts[s] = counts.get(s, 0) + 1
+    gen = torch.Generator().manual_seed(0)
+    muon_cfg = dict(lr=1e-3, beta=0.95, eps=1e-7, weight_decay=0.1, nesterov=True, ns_steps=ns_steps,
+                    adjust_lr_fn="original")
+    total_ms, detail = 0.0, {}
+    for shape, cnt in counts.items():
+        p = nn.Parameter(torch.randn(shape, generator=gen) * 0.02)
+        p.grad = torch.randn(shape, generator=gen) * 1e-3
+        w = ReferenceWrapperCPU([], [p], adam=adam_cfg, muon=muon_cfg)
+        t0 = time.perf_counter()
+        w.step()
+        dt = (time.perf_counter() - t0) * 1e3
+        detail[f"{shape[0]}x{shape[1]}"] = round(dt, 1)
+        total_ms += dt * cnt
+    adam_elems = sum(math.prod(s) for _, s in adam)
+    chunk = 1 << 24
+    p = nn.Parameter(torch.randn(chunk, generator=gen) * 0.02)
+    p.grad = torch.randn(chunk, generator=gen) * 1e-3
+    w = ReferenceWrapperCPU([p], [], adam=adam_cfg, muon=muon_cfg)
+    w.step()
+    t0 = time.perf_counter()
+    w.step()
+    dt = (time.perf_counter() - t0) * 1e3
+    detail["adamw_16M"] = round(dt, 1)
+    total_ms += dt * adam_elems / chunk
+    sample = (f"one matrix per distinct Muon shape ({', '.join(detail)}) through torch.optim.Muon, one 16M-element "
+              f"chunk through torch.optim.AdamW(fused); extrapolated by shape counts and element count")
+    return total_ms, sample, torch.get_num_threads(), detail
+
+
+# ----------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ns-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        run_reference_arm(args, cfg, world)
+        return
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        from datetime import timedelta  # noqa: PLC0415
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        pg = dist.group.WORLD
+
+    from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig  # noqa: PLC0415
+
+    adam_shapes, muon_shapes = cfg["shapes"]()
+    model = ShapedParams(adam_shapes, muon_shapes, dev, seed=0)
+    ggen = torch.Generator(device=dev).manual_seed(1)
+    for p in model.parameters():
+        p.grad = torch.empty_like(p).normal_(0.0, 1e-3, generator=ggen)
+    mcfg = MuonConfig(lr=1e-3, beta=0.95, eps=1e-7, weight_decay=0.1, coeffs=COEFFS, nesterov=True,
+                      ns_steps=args.ns_steps)
+    acfg = AdamConfig(**cfg["adam"])
+    opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg)
+    n_muon, n_adam = len(opt.muon.model_params), len(opt.adamw.model_params)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        opt.step()
+    barrier()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for _ in range(args.steps):
+        opt.step()
+    end.record()
+    barrier()
+    clock_info = clocks.stop()
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = ms_local
+    if world > 1:
+        t = torch.tensor([ms_local], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # Per-kernel timing: one more timed pass with events between every launch.
+    timer = PhaseTimer()
+    opt_branch_timer(opt, timer)
+    barrier()
+    for _ in range(max(1, min(args.steps, 3))):
+        opt.step()
+    barrier()
+    opt_branch_timer(opt, None)
+    per = timer.durations()
+
+    # Work accounting (this rank's share).
+    owned = owned_shapes(opt)
+    flops = {"gram": 0.0, "poly": 0.0, "update": 0.0}
+    elems_muon = 0
+    for s in owned:
+        f = ns_flops_sym(s)
+        for k in flops:
+            flops[k] += f[k]
+        elems_muon += math.prod(s)
+    adam_elems = adam_elems_local(opt)
+    hbm, tf_burst, tf_sus, peak_src = measured_peaks()
+    kernels = {}
+    for k in ("gram", "poly", "update"):
+        d = per.get(k, [])
+        if d:
+            avg = sum(d) / len(d)
+            kernels[f"ns_gemm_{k}"] = {"launches": len(d), "avg_ms": round(avg, 4),
+                                       "tflops": round(flops[k] / (avg * 1e-3) / 1e12, 1),
+                                       "frac_sustained": round(flops[k] / (avg * 1e-3) / 1e12 / tf_sus, 3)}
+    if per.get("adamw"):
+        avg = sum(per["adamw"]) / len(per["adamw"])
+        gbs = 28.0 * adam_elems / (avg * 1e-3) / 1e9
+        kernels["adamw_multi"] = {"launches": len(per["adamw"]), "avg_ms": round(avg, 4), "gbs": round(gbs, 1),
+                                  "frac": round(gbs / hbm, 3), "bytes_per_elem": 28}
+    if per.get("prep"):
+        avg = sum(per["prep"]) / len(per["prep"])
+        gbs = 14.0 * elems_muon / (avg * 1e-3) / 1e9
+        kernels["muon_prep"] = {"launches": len(per["prep"]), "avg_ms": round(avg, 4), "gbs": round(gbs, 1),
+                                "frac": round(gbs / hbm, 3), "bytes_per_elem": 14}
+    ns_ms = sum(sum(per.get(k, [])) for k in ("gram", "poly", "update")) / max(1, len(per.get("update", [1])))
+    ns_total = sum(flops.values())
+    upd = kernels.get("ns_gemm_update", {})
+    traffic = ncu_traffic("ns_gemm_update", args.config)
+    roofline = {"kernel": "ns_gemm_kernel<UPDATE> (tcgen05 B·X + a·X epilogue)", "bound": "tensor",
+                "achieved": upd.get("tflops"), "peak": tf_sus, "unit": "TFLOP/s",
+                "frac": upd.get("frac_sustained"), "peak_kind": f"{peak_src} sustained bf16",
+                "traffic": traffic, "ns_all_tflops": round(ns_total / (ns_ms * 1e-3) / 1e12, 1) if ns_ms else None,
+                "ns_all_frac_sustained": round(ns_total / (ns_ms * 1e-3) / 1e12 / tf_sus, 3) if ns_ms else None,
+                "ns_ms_per_step": round(ns_ms, 3)}
+
+    # End to end: this step's gradients from pinned host memory, result read back.
+    e2e = run_e2e(opt, model, dev, args, barrier, world)
+    launches_per_step = (1 if n_adam else 0) + ((2 + 3 * args.ns_steps) if owned else 0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, cores, detail = cpu_sample(args.config, cfg["adam"], args.ns_steps)
+        cpu = {"value": round(v, 1), "unit": "ms/step", "cores": cores, "kind": "port", "sample": sample,
+               "per_shape_ms": detail}
+
+    if rank == 0:
+        line = {
+            "metric": f"MuonAdamW ms/step ({cfg['name']})", "value": round(ms, 3), "unit": "ms/step",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) params, N(0,1e-3) grads; no dataset)",
+            "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "muon_matrices": n_muon,
+                       "adamw_tensors": n_adam, "ns_steps": args.ns_steps, "coeffs": list(COEFFS),
+                       "parallelism": "single-gpu" if world == 1 else f"muon-owner+zero1-adamw x{world}",
+                       "l2": "inputs (fp32 grads/params/momentum, > 100 GB) exceed L2; no flush needed",
+                       "elementwise_dtype": "fp32"},
+            "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clock_info, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def opt_branch_timer(opt, timer):
+    target = opt.distributed if getattr(opt, "distributed", None) is not None else opt
+    for br in (target.adamw, target.muon):
+        br._timer = timer
+
+
+def owned_shapes(opt):
+    if getattr(opt, "distributed", None) is not None:
+        return opt.distributed.owned_muon_shapes()
+    return [tuple(p.shape) for p in opt.muon.model_params if p.grad is not None]
+
+
+def adam_elems_local(opt):
+    if getattr(opt, "distributed", None) is not None:
+        return opt.distributed.adam_shard_numel()
+    return sum(p.numel() for p in opt.adamw.model_params if p.grad is not None)
+
+
+def ncu_traffic(kernel, config):
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(config, {}).get(kernel)
+    except (ValueError, OSError):
+        return None
+
+
+def run_e2e(opt, model, dev, args, barrier, world):
+    """Same step through the public API, gradients copied from pinned host memory each step."""
+    needed = e2e_grad_tensors(opt, model)
+    total = sum(g.numel() for g in needed)
+    host = torch.empty(total, dtype=torch.float32, pin_memory=True)
+    views, off = [], 0
+    for g in needed:
+        views.append(host[off:off + g.numel()].view_as(g))
+        views[-1].copy_(g)
+        off += g.numel()
+    probe = model.final_norm
+    out = torch.empty(probe.numel(), dtype=torch.float32, pin_memory=True)
+    steps = max(1, args.e2e_steps)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        for g, h in zip(needed, views):
+            g.copy_(h, non_blocking=True)
+        opt.step()
+        out.copy_(probe.detach(), non_blocking=True)
+    end.record()
+    barrier()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": round(ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(total * 4),
+            "d2h_bytes_per_step": int(out.numel() * 4), "steps": steps,
+            "what": "grads H2D (pinned) + MuonAdamW.step() + final-norm params D2H, device-timed"}
+
+
+def e2e_grad_tensors(opt, model):
+    if getattr(opt, "distributed", None) is not None:
+        return opt.distributed.local_grad_tensors()
+    return [p.grad for p in model.parameters() if p.grad is not None]
+
+
+def run_reference_arm(args, cfg, world):
+    """The reference's CPU path on the host cores, bounded sample per step, extrapolated."""
+    vals, sample, cores = [], "", 1
+    for i in range(args.warmup + args.steps):
+        v, sample, cores, _ = cpu_sample(args.config, cfg["adam"], args.ns_steps)
+        if i >= args.warmup:
+            vals.append(v)
+    ms = statistics.mean(vals)
+    line = {"metric": f"MuonAdamW ms/step ({cfg['name']})", "value": round(ms, 1), "unit": "ms/step",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "ns_steps": args.ns_steps,
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(ms, 1), "unit": "ms/step", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(ms, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,166 @@
+/*
+ * muon_adamw_b200.h -- C ABI of the B200 MuonAdamW optimizer step.
+ *
+ * Plain pointers and sizes only.  All pointers named param/grad/exp_avg/
+ * exp_avg_sq/momentum/dev_* are CUDA device pointers; `stream` is a
+ * cudaStream_t passed as void*.  Every function returns 0 (MAD_OK) on success
+ * or a MAD_ERR_* code, with a message from mad_last_error().  No function
+ * allocates device memory: callers size buffers with the *_bytes / *_plan_size
+ * functions and pass them in.
+ *
+ * Each entry point replaces one piece of the reference's Python/Triton path
+ * (reference paths relative to its "MuonAdamW package/" directory):
+ *
+ *   mad_adamw_step         triton_muon_adamw/adamw/triton_adam.py:66-103  solve_adamw_step
+ *   mad_adamw_plan         triton_muon_adamw/adamw/triton_adam.py:106-130 TritonAdamW.__init__ (state binding)
+ *   mad_adamw_step_multi   triton_muon_adamw/adamw/triton_adam.py:132-153 TritonAdamW.step (per-tensor loop)
+ *   mad_muon_plan_size,
+ *   mad_muon_plan          triton_muon_adamw/muon/triton_muon.py:375-412 TritonMuon.__init__ and the
+ *                          per-call workspaces of :319-321 (newton_shultz_step) and :358-359 (muon_step)
+ *   mad_muon_prep          triton_muon_adamw/muon/triton_muon.py:346-356 muon_step prologue
+ *   mad_ns_gram            triton_muon_adamw/muon/triton_muon.py:95-117  solve_ns_kernel_1
+ *   mad_ns_poly            triton_muon_adamw/muon/triton_muon.py:191-212 solve_ns_kernel_2
+ *   mad_ns_update          triton_muon_adamw/muon/triton_muon.py:281-310 solve_ns_kernel_3, and on the
+ *                          last iteration the muon_step epilogue :365-372
+ *   mad_muon_step_multi    triton_muon_adamw/muon/triton_muon.py:414-448 TritonMuon.step
+ */
+#ifndef MUON_ADAMW_B200_H
+#define MUON_ADAMW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MAD_OK = 0,
+  MAD_ERR_INVALID = 1,     /* bad argument: shape, count, null pointer */
+  MAD_ERR_ALIGN = 2,       /* pointer alignment the kernel needs is not met */
+  MAD_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  MAD_ERR_WORKSPACE = 4,   /* caller buffer too small */
+  MAD_ERR_DEVICE = 5       /* a kernel reported an error in its status word */
+};
+
+/* Message describing the last failure on the calling thread ("" if none). */
+const char* mad_last_error(void);
+
+/* ABI version of this library. */
+int32_t mad_abi_version(void);
+
+/* ------------------------------------------------------------------ AdamW */
+
+/* One float32 tensor of the AdamW branch (flattened; any shape). */
+typedef struct mad_adamw_tensor {
+  float* param;
+  const float* grad;
+  float* exp_avg;
+  float* exp_avg_sq;
+  int64_t numel;
+} mad_adamw_tensor;
+
+/* One AdamW update of one tensor, in place (replaces solve_adamw_step,
+ * triton_adam.py:66-103; same argument meaning).  bias1/bias2 are the host
+ * bias corrections 1-beta^t. */
+int mad_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t numel, float lr,
+                   float bias1, float bias2, float beta1, float beta2, float weight_decay, float eps, void* stream);
+
+/* Device bytes of the table mad_adamw_plan writes for these tensors. */
+int mad_adamw_table_bytes(const mad_adamw_tensor* tensors, int32_t n_tensors, int64_t* table_bytes);
+
+/* Writes the multi-tensor table for `tensors` into dev_table and returns its
+ * tile count.  Re-plan whenever any pointer changes (e.g. new .grad tensors).
+ * Synchronises `stream` once (the host staging buffer is freed on return). */
+int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors, void* dev_table, int64_t table_bytes,
+                   int64_t* n_tiles, void* stream);
+
+/* One AdamW update of every planned tensor in one launch (replaces the
+ * TritonAdamW.step per-tensor loop, triton_adam.py:132-153). */
+int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2, float eps,
+                         float weight_decay, float bias1, float bias2, void* stream);
+
+/* ------------------------------------------------------------------ Muon */
+
+/* One float32 Muon matrix (rows x cols, row-major, contiguous). */
+typedef struct mad_muon_matrix {
+  float* param;
+  const float* grad;
+  float* momentum;
+  int64_t rows;
+  int64_t cols;
+  double lr_scale; /* shape adjustment: scaled_lr = float(lr * lr_scale) (triton_muon.py:424-431) */
+} mad_muon_matrix;
+
+/* Sizes and launch counts of a Muon plan; filled by mad_muon_plan_size and
+ * passed back unchanged to every Muon call. */
+typedef struct mad_muon_plan_info {
+  int32_t n_mats;
+  int32_t num_sms;
+  int64_t table_bytes;
+  int64_t work_bytes;
+  int64_t prep_tiles;
+  int64_t gram_tiles;
+  int64_t poly_tiles;
+  int64_t update_tiles;
+  int64_t off_mats;
+  int64_t off_tmaps;
+  int64_t off_gram_tiles;
+  int64_t off_poly_tiles;
+  int64_t off_update_tiles;
+  int64_t off_prep_map;
+  int64_t off_partials;
+} mad_muon_plan_info;
+
+/* Where one matrix's Newton-Schulz operands live inside the work buffer. */
+typedef struct mad_muon_buffers {
+  void* x[2];       /* bf16 m x n iterate (ping, pong), leading dim ld_x */
+  void* gram;       /* bf16 m x m, leading dim ld_mm */
+  void* poly;       /* bf16 m x m, leading dim ld_mm */
+  int64_t m, n, ld_x, ld_mm;
+  int32_t transposed;
+} mad_muon_buffers;
+
+/* Computes table/work sizes and tile counts for these matrices. */
+int mad_muon_plan_size(const mad_muon_matrix* mats, int32_t n_mats, mad_muon_plan_info* info);
+
+/* Writes the plan (matrix descriptors, TMA tensor maps, tile lists) into
+ * dev_table and lays the bf16 workspaces out in dev_work.  If `buffers` is
+ * non-null it receives n_mats entries describing the workspace layout.
+ * Synchronises `stream` once. */
+int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* dev_table, void* dev_work,
+                  const mad_muon_plan_info* info, mad_muon_buffers* buffers, void* stream);
+
+/* Momentum EMA, Nesterov, bf16 cast, transpose-to-wide and the Frobenius
+ * norm of every planned matrix, in one launch. */
+int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, float beta, int32_t nesterov, float eps,
+                  void* stream);
+
+/* Newton-Schulz iteration `iter` (0-based), one launch each:
+ *   gram:   A  = s² X Xᵀ          upper-triangle tiles, mirrored
+ *   poly:   B  = b A + c A A      upper-triangle tiles, mirrored
+ *   update: X' = s (a X + B X)    s = 1/||X|| on iteration 0, else 1
+ * With last != 0 the update writes the parameters instead of X':
+ *   p = p - float(lr*weight_decay) p ;  p = p - float(lr*lr_scale) * bf16(X')
+ * with X' transposed back to the parameter's orientation for tall matrices. */
+int mad_ns_gram(const mad_muon_plan_info* info, void* dev_table, int32_t iter, void* stream);
+int mad_ns_poly(const mad_muon_plan_info* info, void* dev_table, int32_t iter, float b, float c, void* stream);
+int mad_ns_update(const mad_muon_plan_info* info, void* dev_table, int32_t iter, int32_t last, float a, double lr,
+                  double weight_decay, void* stream);
+
+/* The whole Muon branch for every planned matrix: prep, then ns_steps x
+ * (gram, poly, update), the last update writing the parameters. */
+int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, float beta, int32_t nesterov, float a,
+                        float b, float c, int32_t ns_steps, float eps, double lr, double weight_decay, void* stream);
+
+/* Copies the plan's device status word to *status (synchronises `stream`)
+ * and, if clear != 0, resets it.  Non-zero bits mean a kernel gave up
+ * waiting on a barrier; the step's results are then invalid. */
+int mad_muon_read_status(const mad_muon_plan_info* info, void* dev_table, uint32_t* status, int32_t clear,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUON_ADAMW_B200_H */

@@ -1,0 +1,330 @@
+"""CPU oracle for the MuonAdamW optimizer step.  TEST INFRASTRUCTURE ONLY.
+
+This module restates, with plain torch CPU arithmetic, the algorithm of the
+reference project Mithun-033/Triton-MuonAdamW for its one hot path,
+``MuonAdamW.step()``.  It is the *checker*: only ``tests/``, the repository's
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import it.  The
+shipped optimizer (``triton_muon_adamw``) never imports it and has no CPU path.
+
+Reference paths below are relative to the reference project root; ``PKG`` is
+its ``MuonAdamW package/`` directory.
+
+Two restatements live here:
+
+* ``OracleMuonAdamW`` follows the reference's *Triton* path
+  (``PKG/triton_muon_adamw/optimizer.py:70-175`` routing,
+  ``PKG/triton_muon_adamw/adamw/triton_adam.py`` AdamW,
+  ``PKG/triton_muon_adamw/muon/triton_muon.py`` Muon) with every bf16 rounding
+  point of that path made explicit and every matrix product accumulated in
+  float64, so its result does not depend on the host's BLAS blocking.
+* ``ReferenceWrapperCPU`` follows the reference's comparison wrapper
+  ``PyTorchMuonAdamW`` (``optimizer.py:178-260``), i.e. ``torch.optim.AdamW``
+  (fused) and ``torch.optim.Muon`` running on the host cores.  It is the CPU
+  baseline that ``bench.py`` times.
+
+Parity pin: ``tests/golden/make_golden.py`` imports the reference package in
+the development container and records its outputs (``PyTorchMuonAdamW`` on CPU,
+``TritonAdamW`` under the Triton interpreter) into ``tests/golden/``;
+``tests/test_oracle_golden.py`` checks both restatements against them.  The
+reference's Newton-Schulz Triton kernels do not run in the Triton 3.6
+interpreter (bf16 is unsupported there), so the Triton-path Muon restatement is
+pinned through the wrapper goldens (same rounding points, same coefficients)
+rather than through the Triton kernels themselves.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+# Newton-Schulz coefficients torch.optim.Muon uses by default; the reference
+# wrapper does not forward its own coefficients (optimizer.py:228-236), so these
+# are what PyTorchMuonAdamW computes with.
+TORCH_MUON_COEFFS = (3.4445, -4.7750, 2.0315)
+
+
+def bf16_round(x: torch.Tensor) -> torch.Tensor:
+    """Round to bfloat16 (round-to-nearest-even) and return as float32."""
+    return x.to(torch.bfloat16).to(torch.float32)
+
+
+# --------------------------------------------------------------------------
+# AdamW branch  (triton_adam.py)
+# --------------------------------------------------------------------------
+
+def adamw_update_(p, g, m, v, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2):
+    """One elementwise AdamW update in float32, in place on ``p``, ``m``, ``v``.
+
+    Follows ``triton_adam.py:53-63``: moments first, then bias-corrected
+    moments, then decoupled decay applied multiplicatively to the old value.
+    """
+    f = torch.float32
+    m_t = (torch.tensor(beta1, dtype=f) * m) + (torch.tensor(1.0 - beta1, dtype=f) * g)
+    v_t = (torch.tensor(beta2, dtype=f) * v) + (torch.tensor(1.0 - beta2, dtype=f) * (g * g))
+    m_c = m_t / torch.tensor(bias1, dtype=f)
+    v_c = v_t / torch.tensor(bias2, dtype=f)
+    decayed = torch.tensor(1.0 - lr * weight_decay, dtype=f) * p
+    p.copy_(decayed - torch.tensor(lr, dtype=f) * (m_c / (torch.sqrt(v_c) + torch.tensor(eps, dtype=f))))
+    m.copy_(m_t)
+    v.copy_(v_t)
+
+
+def adamw_bias_corrections(beta1: float, beta2: float, step: int) -> tuple[float, float]:
+    """Host bias corrections with the branch-global step count (triton_adam.py:137-148)."""
+    return 1.0 - beta1 ** step, 1.0 - beta2 ** step
+
+
+# --------------------------------------------------------------------------
+# Muon branch  (triton_muon.py)
+# --------------------------------------------------------------------------
+
+def muon_momentum_(grad: torch.Tensor, mom: torch.Tensor, beta: float, nesterov: bool) -> torch.Tensor:
+    """Momentum EMA in place on ``mom`` and the (optionally Nesterov) update.
+
+    ``triton_muon.py:346``: ``mom = beta*mom + (1-beta)*grad`` (buffer updated);
+    ``triton_muon.py:348-349``: Nesterov returns ``grad + beta*(mom - grad)``
+    as a new tensor and leaves the buffer alone.
+    """
+    f = torch.float32
+    mom.copy_(mom * torch.tensor(beta, dtype=f) + grad * torch.tensor(1.0 - beta, dtype=f))
+    if nesterov:
+        return grad + torch.tensor(beta, dtype=f) * (mom - grad)
+    return mom.clone()
+
+
+def to_wide_bf16(u: torch.Tensor) -> tuple[torch.Tensor, bool]:
+    """bf16 cast, then transpose tall matrices so rows <= cols (triton_muon.py:351-354)."""
+    x = bf16_round(u)
+    transposed = x.shape[0] > x.shape[1]
+    if transposed:
+        x = x.t().contiguous()
+    return x, transposed
+
+
+def frobenius_normalize(x: torch.Tensor, eps: float) -> tuple[torch.Tensor, float]:
+    """``X / max(||X||_F, eps)`` with the reference's bf16 rounding points.
+
+    ``triton_muon.py:356`` divides a bf16 tensor by its bf16 norm: the norm is
+    accumulated in float32 and rounded to bf16, clamped, and each quotient is
+    rounded to bf16.  Returns the normalised matrix and the bf16 norm used.
+    """
+    sumsq = float((x.double() * x.double()).sum())
+    norm = float(bf16_round(torch.tensor(math.sqrt(sumsq), dtype=torch.float32)))
+    norm = max(norm, float(bf16_round(torch.tensor(eps, dtype=torch.float32))))
+    return bf16_round(x / torch.tensor(norm, dtype=torch.float32)), norm
+
+
+def ns_iteration(x: torch.Tensor, a: float, b: float, c: float) -> torch.Tensor:
+    """One Newton-Schulz iteration (triton_muon.py:313-325).
+
+    Each product is bf16 x bf16 accumulated wide and rounded once to bf16, the
+    way the three reference kernels do it:
+
+    * ``A  = bf16(X Xᵀ)``                 -- ns_kernel_1, triton_muon.py:35-93
+    * ``B  = bf16(b A + c (A Aᵀ))``       -- ns_kernel_2, triton_muon.py:119-188
+    * ``X' = bf16(a X + B X)``            -- ns_kernel_3, triton_muon.py:215-278
+    """
+    xd = x.double()
+    A = bf16_round((xd @ xd.t()).float())
+    Ad = A.double()
+    B = bf16_round((b * Ad + c * (Ad @ Ad.t())).float())
+    return bf16_round((a * xd + B.double() @ xd).float())
+
+
+def orthogonalize(u: torch.Tensor, coeffs, ns_steps: int, eps: float) -> torch.Tensor:
+    """bf16 orthogonalised update in the parameter's orientation (triton_muon.py:351-366)."""
+    a, b, c = coeffs
+    x, transposed = to_wide_bf16(u)
+    x, _ = frobenius_normalize(x, eps)
+    for _ in range(ns_steps):
+        x = ns_iteration(x, a, b, c)
+    return x.t() if transposed else x
+
+
+def scaled_lr(lr: float, shape, adjust_lr_fn: str) -> float:
+    """Shape-dependent Muon learning rate (triton_muon.py:424-431).
+
+    ``match_rms_adamw`` raises in the reference (``max`` of an int); it is
+    restated as torch's definition ``0.2*lr*sqrt(max(rows, cols))``.
+    """
+    rows, cols = shape[0], shape[1]
+    if adjust_lr_fn == "original":
+        return lr * math.sqrt(max(1.0, rows / cols))
+    if adjust_lr_fn == "match_rms_adamw":
+        return 0.2 * lr * math.sqrt(max(rows, cols))
+    if adjust_lr_fn == "spectral_unclamped":
+        return lr * math.sqrt(rows / cols)
+    raise AssertionError(f"Invalid adjust_lr_fn: {adjust_lr_fn}")
+
+
+def muon_apply_(p: torch.Tensor, o: torch.Tensor, lr: float, weight_decay: float, slr: float) -> None:
+    """Decoupled decay then the scaled update, as two float32 subtractions (triton_muon.py:368-372)."""
+    f = torch.float32
+    p.sub_(torch.tensor(lr * weight_decay, dtype=f) * p)
+    p.sub_(torch.tensor(slr, dtype=f) * o.to(f))
+
+
+def muon_matrix_step_(p, g, mom, *, lr, beta, nesterov, coeffs, ns_steps, eps, weight_decay,
+                      adjust_lr_fn="original") -> torch.Tensor:
+    """Full Muon update of one matrix (triton_muon.py:327-372, lr from :424-431).
+
+    Returns the bf16-valued orthogonalised update so tests can compare it
+    directly, not only through ``lr``-scaled parameters.
+    """
+    u = muon_momentum_(g, mom, beta, nesterov)
+    o = orthogonalize(u, coeffs, ns_steps, eps)
+    muon_apply_(p, o, lr, weight_decay, scaled_lr(lr, p.shape, adjust_lr_fn))
+    return o
+
+
+# --------------------------------------------------------------------------
+# Routing  (optimizer.py)
+# --------------------------------------------------------------------------
+
+def split_params(model=None, explicit=None):
+    """Parameter routing of ``MuonAdamW.__init__`` (optimizer.py:107-130).
+
+    Auto mode: 2-D trainable parameters that are neither the input embedding
+    nor the output head go to Muon, everything else to AdamW; parameters that
+    share storage are taken once.
+    """
+    if explicit is not None:
+        return list(explicit.get("adam", [])), list(explicit.get("muon", []))
+    embed = model.get_input_embeddings().weight
+    out = model.get_output_embeddings()
+    head = out.weight if out is not None else None
+    adam, muon, seen = [], [], set()
+    for p in model.parameters():
+        if not p.requires_grad or p.data_ptr() in seen:
+            continue
+        seen.add(p.data_ptr())
+        if p.ndim == 2 and p is not embed and p is not head:
+            muon.append(p)
+        else:
+            adam.append(p)
+    return adam, muon
+
+
+@dataclass
+class OracleMuonAdamW:
+    """CPU restatement of ``MuonAdamW`` (optimizer.py:70-175) over float32 tensors.
+
+    Holds its own copies of the parameters (``params_adam``/``params_muon``)
+    and their gradients; ``step()`` is AdamW then Muon (optimizer.py:156-159).
+    """
+
+    params_adam: list
+    params_muon: list
+    adam: dict = field(default_factory=dict)   # lr, betas, eps, weight_decay
+    muon: dict = field(default_factory=dict)   # lr, beta, eps, weight_decay, coeffs, nesterov, ns_steps, adjust_lr_fn
+    step_num: int = 0
+
+    def __post_init__(self):
+        self.exp_avg = [torch.zeros_like(p, dtype=torch.float32) for p in self.params_adam]
+        self.exp_avg_sq = [torch.zeros_like(p, dtype=torch.float32) for p in self.params_adam]
+        self.momentum = [torch.zeros_like(p) for p in self.params_muon]
+        self.last_updates = [None] * len(self.params_muon)
+
+    def step(self, grads_adam, grads_muon):
+        self.step_num += 1
+        b1, b2 = self.adam["betas"]
+        bias1, bias2 = adamw_bias_corrections(b1, b2, self.step_num)
+        for p, g, m, v in zip(self.params_adam, grads_adam, self.exp_avg, self.exp_avg_sq):
+            if g is None:
+                continue
+            adamw_update_(p, g, m, v, lr=self.adam["lr"], beta1=b1, beta2=b2, eps=self.adam["eps"],
+                          weight_decay=self.adam["weight_decay"], bias1=bias1, bias2=bias2)
+        mc = self.muon
+        for i, (p, g, mom) in enumerate(zip(self.params_muon, grads_muon, self.momentum)):
+            if g is None:
+                continue
+            self.last_updates[i] = muon_matrix_step_(
+                p, g, mom, lr=mc["lr"], beta=mc["beta"], nesterov=mc["nesterov"], coeffs=mc["coeffs"],
+                ns_steps=mc["ns_steps"], eps=mc["eps"], weight_decay=mc["weight_decay"],
+                adjust_lr_fn=mc.get("adjust_lr_fn", "original"))
+
+
+class ReferenceWrapperCPU:
+    """Host-core restatement of ``PyTorchMuonAdamW`` (optimizer.py:178-260).
+
+    Builds ``torch.optim.AdamW(fused=True)`` and ``torch.optim.Muon`` over the
+    given CPU parameters exactly as the wrapper does -- including not
+    forwarding the Muon coefficients or eps (optimizer.py:228-236) -- so its
+    results are the wrapper's results.
+    """
+
+    def __init__(self, adam_params, muon_params, *, adam: dict, muon: dict):
+        self.adamw = torch.optim.AdamW(adam_params, lr=adam["lr"], betas=adam["betas"],
+                                       weight_decay=adam["weight_decay"], eps=adam["eps"],
+                                       fused=True) if adam_params else None
+        self.muon = torch.optim.Muon(muon_params, lr=muon["lr"], momentum=muon["beta"],
+                                     weight_decay=muon["weight_decay"], nesterov=muon["nesterov"],
+                                     ns_steps=muon["ns_steps"],
+                                     adjust_lr_fn=muon.get("adjust_lr_fn", "original")) if muon_params else None
+
+    def step(self):
+        if self.adamw is not None:
+            self.adamw.step()
+        if self.muon is not None:
+            self.muon.step()
+
+
+# --------------------------------------------------------------------------
+# Synthetic parameter sets  (BASELINE.json configs)
+# --------------------------------------------------------------------------
+
+def gpt_c1_shapes(d=512, layers=4, ffn=2048, vocab=8192):
+    """Parameter shapes of the CPU-runnable config: a GPT decoder with tied embeddings.
+
+    Returns ``(adam_shapes, muon_shapes)``: the tied embedding, LayerNorm
+    weights/biases and linear biases go to AdamW, the block weights to Muon.
+    At the defaults this is 16.8M parameters.
+    """
+    adam = [(vocab, d)]                     # token embedding, tied with the head
+    muon = []
+    for _ in range(layers):
+        adam += [(d,), (d,)]                # ln1
+        for _ in range(4):                  # q, k, v, o projections
+            muon.append((d, d))
+            adam.append((d,))
+        adam += [(d,), (d,)]                # ln2
+        muon.append((ffn, d))               # fc
+        adam.append((ffn,))
+        muon.append((d, ffn))               # proj
+        adam.append((d,))
+    adam += [(d,), (d,)]                    # final ln
+    return adam, muon
+
+
+def llama_shapes(d, layers, n_heads, n_kv_heads, ffn, vocab):
+    """Parameter shapes of a Llama-style decoder with an untied head (RMSNorm, SwiGLU).
+
+    Position embedding is rotary (no parameters); embeddings, head and norms go
+    to AdamW, the seven block matrices per layer to Muon.
+    """
+    hd = d // n_heads
+    adam = [(vocab, d), (vocab, d)]
+    muon = []
+    for _ in range(layers):
+        adam += [(d,), (d,)]
+        muon += [(n_heads * hd, d), (n_kv_heads * hd, d), (n_kv_heads * hd, d), (d, n_heads * hd),
+                 (ffn, d), (ffn, d), (d, ffn)]
+    adam.append((d,))
+    return adam, muon
+
+
+def llama_8b_shapes():
+    return llama_shapes(4096, 32, 32, 8, 14336, 128256)
+
+
+def llama_1b3_shapes():
+    return llama_shapes(2048, 24, 16, 16, 5504, 32000)
+
+
+def ns_flops(shape, ns_steps: int, symmetric: bool = True) -> float:
+    """Newton-Schulz flops for one matrix: per iteration 3m²n+m³ (triangles) or 4m²n+2m³ (dense)."""
+    m, n = min(shape), max(shape)
+    per = 3 * m * m * n + m ** 3 if symmetric else 4 * m * m * n + 2 * m ** 3
+    return float(per) * ns_steps

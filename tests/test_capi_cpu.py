@@ -1,0 +1,175 @@
+"""CPU checks of the C-ABI library and the host-side Python layer (no GPU needed).
+
+No compute call is made here: only loading, symbol export, argument
+validation (which fails before any CUDA call) and plan sizing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+import torch.nn as nn
+
+from conftest import REPO
+
+HEADER = REPO / "include" / "muon_adamw_b200.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mad_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    from triton_muon_adamw import _lib
+    lib = _lib.load()
+    declared = header_functions()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in {HEADER.name} but not exported"
+    assert set(declared) == set(_lib.SIGNATURES), "ctypes signatures must cover exactly the header"
+    assert lib.mad_abi_version() == 1
+
+
+def test_invalid_arguments_fail_before_any_cuda_call():
+    from triton_muon_adamw import _lib
+    lib = _lib.load()
+    rc = lib.mad_adamw_step(None, None, None, None, -1, 1e-3, 0.1, 0.1, 0.9, 0.999, 0.0, 1e-8, None)
+    assert rc == 1 and b"negative numel" in lib.mad_last_error()
+    rc = lib.mad_adamw_step(None, None, None, None, 10, 1e-3, 0.1, 0.1, 0.9, 0.999, 0.0, 1e-8, None)
+    assert rc == 1 and b"null pointer" in lib.mad_last_error()
+    # zero elements is a no-op, not an error
+    assert lib.mad_adamw_step(None, None, None, None, 0, 1e-3, 0.1, 0.1, 0.9, 0.999, 0.0, 1e-8, None) == 0
+    info = _lib.MuonPlanInfo()
+    bad = (_lib.MuonMatrix * 1)(_lib.MuonMatrix(8, 8, 8, 0, 4, 1.0))
+    assert lib.mad_muon_plan_size(bad, 1, ctypes.byref(info)) == 1
+    assert b"shape" in lib.mad_last_error()
+    assert lib.mad_muon_step_multi(ctypes.byref(info), None, 0.95, 1, 3.4, -4.7, 2.0, 0, 1e-7, 1e-3, 0.1, None) == 1
+
+
+def test_plan_sizes_for_the_8b_shapes():
+    """Tile counts of the plan follow from the shapes alone (upper-triangle tiles only)."""
+    from oracle.muon_adamw_oracle import llama_8b_shapes
+    from triton_muon_adamw import _lib
+    lib = _lib.load()
+    _, muon = llama_8b_shapes()
+    arr = (_lib.MuonMatrix * len(muon))()
+    for i, (r, c) in enumerate(muon):
+        arr[i] = _lib.MuonMatrix(16, 16, 16, r, c, 1.0)     # fake, aligned, never dereferenced
+    info = _lib.MuonPlanInfo()
+    _lib.check(lib.mad_muon_plan_size(arr, len(muon), ctypes.byref(info)))
+
+    def tri(m):
+        tms, tns = -(-m // 128), -(-m // 256)
+        return sum(min(tms, 2 * tn + 2) for tn in range(tns))
+
+    counts = {}
+    for s in muon:
+        counts[s] = counts.get(s, 0) + 1
+    exp_gram = sum(cnt * tri(min(s)) for s, cnt in counts.items())
+    exp_upd = sum(cnt * (-(-min(s) // 128)) * (-(-max(s) // 256)) for s, cnt in counts.items())
+    assert info.gram_tiles == exp_gram == info.poly_tiles
+    assert info.update_tiles == exp_upd
+    # bf16 workspaces: 2 iterates (m x n) + A, B (m x m), rows padded to 64
+    exp_work = sum(cnt * (2 * min(s) * max(s) * 2 + 2 * min(s) ** 2 * 2) for s, cnt in counts.items())
+    assert info.work_bytes == exp_work
+    assert info.table_bytes < 64 << 20
+
+
+class Tiny(nn.Module):
+    def __init__(self, tied=True):
+        super().__init__()
+        self.emb = nn.Embedding(32, 8)
+        self.l1 = nn.Linear(8, 16)
+        self.ln = nn.LayerNorm(16)
+        self.l2 = nn.Linear(16, 8, bias=False)
+        self.head = nn.Linear(8, 32, bias=False)
+        if tied:
+            self.head.weight = self.emb.weight
+        self.frozen = nn.Parameter(torch.zeros(4, 4), requires_grad=False)
+
+    def get_input_embeddings(self):
+        return self.emb
+
+    def get_output_embeddings(self):
+        return self.head
+
+
+@pytest.mark.parametrize("tied", [True, False])
+def test_auto_split_matches_reference_routing(tied):
+    from oracle.muon_adamw_oracle import split_params
+    from triton_muon_adamw.optimizer import split_parameters
+    m = Tiny(tied)
+    adam, muon = split_parameters(m, "auto")
+    ref_adam, ref_muon = split_params(model=m)
+    assert [id(p) for p in adam] == [id(p) for p in ref_adam]
+    assert [id(p) for p in muon] == [id(p) for p in ref_muon]
+    assert [tuple(p.shape) for p in muon] == [(16, 8), (8, 16)]
+    assert sum(p is m.emb.weight for p in adam) == 1
+
+
+def test_split_errors_match_reference():
+    from triton_muon_adamw.optimizer import split_parameters
+    with pytest.raises(ValueError, match="explicit"):
+        split_parameters(Tiny(), "explicit")
+    with pytest.raises(ValueError, match="auto"):
+        split_parameters({"adam": [], "muon": []}, "auto")
+    with pytest.raises(AttributeError):
+        split_parameters(nn.Linear(2, 2), "auto")
+
+
+def test_configs_match_reference_defaults():
+    """Field names, order and defaults of optimizer.py:14-67 in the reference."""
+    from dataclasses import fields
+    from triton_muon_adamw import AdamConfig, MuonConfig
+    assert [(f.name, f.default) for f in fields(AdamConfig)] == [
+        ("lr", 1e-3), ("betas", (0.9, 0.999)), ("eps", 1e-7), ("weight_decay", 0.01)]
+    assert [(f.name, f.default) for f in fields(MuonConfig)] == [
+        ("lr", 1e-3), ("beta", 0.95), ("eps", 1e-7), ("weight_decay", 0.1), ("coeffs", (3.445, -4.775, 2.0315)),
+        ("nesterov", True), ("ns_steps", 5), ("adjust_lr_fn", "original")]
+
+
+def test_bad_adjust_lr_fn_raises_assertion():
+    from triton_muon_adamw import MuonAdamW, MuonConfig
+    with pytest.raises(AssertionError):
+        MuonAdamW({"adam": [], "muon": []}, muon_config=MuonConfig(adjust_lr_fn="bogus"), parameter_split="explicit")
+
+
+def test_product_path_refuses_cpu_tensors():
+    """There is no CPU implementation: a CPU parameter fails loudly at step()."""
+    from triton_muon_adamw import MuonAdamW
+    m = Tiny()
+    for p in m.parameters():
+        p.grad = torch.zeros_like(p)
+    opt = MuonAdamW(m)
+    with pytest.raises(ValueError, match="CUDA"):
+        opt.step()
+
+
+def test_lr_scale_matches_oracle():
+    from oracle.muon_adamw_oracle import scaled_lr
+    from triton_muon_adamw.muon.cuda_muon import lr_scale
+    for fn in ("original", "match_rms_adamw", "spectral_unclamped"):
+        for shape in [(4096, 1024), (1024, 4096), (7, 7), (14336, 4096)]:
+            assert 1e-3 * lr_scale(shape, fn) == pytest.approx(scaled_lr(1e-3, shape, fn), rel=1e-15)
+
+
+def test_state_dict_layout_matches_torch_wrapper():
+    """state_dict() of MuonAdamW has the layout of PyTorchMuonAdamW.state_dict() (CPU, before any step)."""
+    from triton_muon_adamw import MuonAdamW, PyTorchMuonAdamW
+    m = Tiny()
+    ours = MuonAdamW(m).state_dict()
+    ref = PyTorchMuonAdamW(Tiny()).state_dict()
+    assert set(ours) == set(ref) == {"adam", "muon"}
+    for k in ("adam", "muon"):
+        assert set(ours[k]) == set(ref[k])
+        og, rg = ours[k]["param_groups"][0], ref[k]["param_groups"][0]
+        assert og["params"] == rg["params"]
+        for key in ("lr", "weight_decay"):
+            assert og[key] == rg[key]
+    assert set(ours["muon"]["state"][0]) == {"momentum_buffer"}

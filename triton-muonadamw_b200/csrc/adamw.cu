@@ -1,0 +1,245 @@
+// AdamW branch: one elementwise fp32 update of param, exp_avg, exp_avg_sq.
+//
+// Follows the reference kernel's formula (triton_adam.py:53-63):
+//   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g²
+//   p = (1 - lr wd) p - lr (m/bias1) / (sqrt(v/bias2) + eps)
+// with every product and sum rounded separately (no FMA contraction) so it
+// agrees with the float32 CPU oracle to the last few ulps.
+//
+// Layout: a multi-tensor launch walks a table of tensors cut into 4096-element
+// tiles; a tile -> tensor index map (int32 per tile) sits in front of the
+// AdamEntry array, so each CTA finds its tensor with one load.  Each thread
+// moves 4 float4 of each of p, g, m, v per tile (16 B x 4 streams in flight),
+// which is what the HBM3e streaming roofline needs: 28 bytes per element.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "capi_common.h"
+#include "plan.cuh"
+
+namespace mad {
+
+struct AdamScalars {
+  float lr, beta1, beta2, one_m_beta1, one_m_beta2, eps, decay, bias1, bias2;
+};
+
+__device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v, const AdamScalars& s) {
+  const float mt = __fadd_rn(__fmul_rn(s.beta1, m), __fmul_rn(s.one_m_beta1, g));
+  const float vt = __fadd_rn(__fmul_rn(s.beta2, v), __fmul_rn(s.one_m_beta2, __fmul_rn(g, g)));
+  const float mc = __fdiv_rn(mt, s.bias1);
+  const float vc = __fdiv_rn(vt, s.bias2);
+  const float step = __fdiv_rn(mc, __fadd_rn(__fsqrt_rn(vc), s.eps));
+  p = __fsub_rn(__fmul_rn(s.decay, p), __fmul_rn(s.lr, step));
+  m = mt;
+  v = vt;
+}
+
+__device__ __forceinline__ void adam_vec(float4& p, const float4& g, float4& m, float4& v, const AdamScalars& s) {
+  adam_elem(p.x, g.x, m.x, v.x, s);
+  adam_elem(p.y, g.y, m.y, v.y, s);
+  adam_elem(p.z, g.z, m.z, v.z, s);
+  adam_elem(p.w, g.w, m.w, v.w, s);
+}
+
+// One tile [off, off+len) of one tensor.  Full aligned tiles take the
+// 16-loads-in-flight path; ragged or misaligned pieces take a generic loop.
+__device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
+  float* __restrict__ p = e.p + off;
+  const float* __restrict__ g = e.g + off;
+  float* __restrict__ m = e.m + off;
+  float* __restrict__ v = e.v + off;
+  const int t = threadIdx.x;
+  if (e.vec && len == ADAM_TILE) {
+    float4 rp[4], rg[4], rm[4], rv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = i * ADAM_THREADS + t;
+      rp[i] = __ldcs(reinterpret_cast<const float4*>(p) + idx);
+      rg[i] = __ldcs(reinterpret_cast<const float4*>(g) + idx);
+      rm[i] = __ldcs(reinterpret_cast<const float4*>(m) + idx);
+      rv[i] = __ldcs(reinterpret_cast<const float4*>(v) + idx);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      adam_vec(rp[i], rg[i], rm[i], rv[i], s);
+      const int idx = i * ADAM_THREADS + t;
+      __stcs(reinterpret_cast<float4*>(p) + idx, rp[i]);
+      __stcs(reinterpret_cast<float4*>(m) + idx, rm[i]);
+      __stcs(reinterpret_cast<float4*>(v) + idx, rv[i]);
+    }
+    return;
+  }
+  const int nvec = e.vec ? (len >> 2) : 0;
+  for (int i = t; i < nvec; i += ADAM_THREADS) {
+    float4 a = __ldcs(reinterpret_cast<const float4*>(p) + i);
+    float4 b = __ldcs(reinterpret_cast<const float4*>(g) + i);
+    float4 c = __ldcs(reinterpret_cast<const float4*>(m) + i);
+    float4 d = __ldcs(reinterpret_cast<const float4*>(v) + i);
+    adam_vec(a, b, c, d, s);
+    __stcs(reinterpret_cast<float4*>(p) + i, a);
+    __stcs(reinterpret_cast<float4*>(m) + i, c);
+    __stcs(reinterpret_cast<float4*>(v) + i, d);
+  }
+  for (int i = nvec * 4 + t; i < len; i += ADAM_THREADS) {
+    float a = p[i], c = m[i], d = v[i];
+    adam_elem(a, g[i], c, d, s);
+    p[i] = a;
+    m[i] = c;
+    v[i] = d;
+  }
+}
+
+__global__ void __launch_bounds__(ADAM_THREADS) adamw_multi_kernel(const AdamEntry* __restrict__ entries,
+                                                                   const int32_t* __restrict__ tile_map,
+                                                                   int64_t n_tiles, AdamScalars s) {
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const AdamEntry e = entries[tile_map[tile]];
+    const int64_t off = (tile - e.tile_begin) * ADAM_TILE;
+    const int64_t rem = e.numel - off;
+    const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
+    adam_tile(e, off, len, s);
+  }
+}
+
+__global__ void __launch_bounds__(ADAM_THREADS) adamw_single_kernel(AdamEntry e, int64_t n_tiles, AdamScalars s) {
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int64_t off = tile * ADAM_TILE;
+    const int64_t rem = e.numel - off;
+    const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
+    adam_tile(e, off, len, s);
+  }
+}
+
+static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, float wd, float bias1, float bias2) {
+  AdamScalars s;
+  s.lr = lr;
+  s.beta1 = beta1;
+  s.beta2 = beta2;
+  s.one_m_beta1 = static_cast<float>(1.0 - static_cast<double>(beta1));
+  s.one_m_beta2 = static_cast<float>(1.0 - static_cast<double>(beta2));
+  s.eps = eps;
+  s.decay = static_cast<float>(1.0 - static_cast<double>(lr) * static_cast<double>(wd));
+  s.bias1 = bias1;
+  s.bias2 = bias2;
+  return s;
+}
+
+static int adam_grid(int64_t n_tiles) {
+  // 8 resident CTAs of 256 threads per SM; a grid-stride loop covers the rest.
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n_tiles, cap)));
+}
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Table layout: int32 tile map [n_tiles] at offset 0, then the AdamEntry array
+// at the next 256-byte boundary.  Both offsets follow from n_tiles alone, so a
+// step call needs only the table pointer and the tile count.
+static int64_t entries_offset(int64_t n_tiles) {
+  return (n_tiles * static_cast<int64_t>(sizeof(int32_t)) + 255) / 256 * 256;
+}
+
+static int64_t table_layout(int32_t n, int64_t n_tiles) {
+  return entries_offset(n_tiles) + static_cast<int64_t>(n) * static_cast<int64_t>(sizeof(AdamEntry));
+}
+
+}  // namespace mad
+
+using namespace mad;
+
+extern "C" int mad_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t numel,
+                              float lr, float bias1, float bias2, float beta1, float beta2, float weight_decay,
+                              float eps, void* stream) {
+  clear_error();
+  if (numel < 0) return fail(MAD_ERR_INVALID, "mad_adamw_step: negative numel");
+  if (numel == 0) return MAD_OK;
+  if (!param || !grad || !exp_avg || !exp_avg_sq) return fail(MAD_ERR_INVALID, "mad_adamw_step: null pointer");
+  if (!(bias1 > 0.f) || !(bias2 > 0.f)) return fail(MAD_ERR_INVALID, "mad_adamw_step: bias corrections must be > 0");
+  AdamEntry e{};
+  e.p = param;
+  e.g = grad;
+  e.m = exp_avg;
+  e.v = exp_avg_sq;
+  e.numel = numel;
+  e.tile_begin = 0;
+  e.vec = aligned16(param) && aligned16(grad) && aligned16(exp_avg) && aligned16(exp_avg_sq);
+  const int64_t n_tiles = (numel + ADAM_TILE - 1) / ADAM_TILE;
+  adamw_single_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      e, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
+  return check_launch("adamw_single_kernel");
+}
+
+extern "C" int mad_adamw_table_bytes(const mad_adamw_tensor* tensors, int32_t n_tensors, int64_t* table_bytes) {
+  clear_error();
+  if (n_tensors < 0 || (n_tensors > 0 && !tensors) || !table_bytes)
+    return fail(MAD_ERR_INVALID, "mad_adamw_table_bytes: bad arguments");
+  int64_t tiles = 0;
+  for (int32_t i = 0; i < n_tensors; ++i) {
+    if (tensors[i].numel < 0) return fail(MAD_ERR_INVALID, "mad_adamw_table_bytes: negative numel");
+    tiles += (tensors[i].numel + ADAM_TILE - 1) / ADAM_TILE;
+  }
+  *table_bytes = table_layout(n_tensors, tiles);
+  return MAD_OK;
+}
+
+extern "C" int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors, void* dev_table,
+                              int64_t table_bytes, int64_t* n_tiles_out, void* stream) {
+  clear_error();
+  if (n_tensors < 0 || (n_tensors > 0 && !tensors) || !n_tiles_out || (n_tensors > 0 && !dev_table))
+    return fail(MAD_ERR_INVALID, "mad_adamw_plan: bad arguments");
+  std::vector<AdamEntry> entries(n_tensors);
+  int64_t tiles = 0;
+  for (int32_t i = 0; i < n_tensors; ++i) {
+    const mad_adamw_tensor& t = tensors[i];
+    if (t.numel < 0) return fail(MAD_ERR_INVALID, "mad_adamw_plan: negative numel");
+    if (t.numel > 0 && (!t.param || !t.grad || !t.exp_avg || !t.exp_avg_sq))
+      return fail(MAD_ERR_INVALID, "mad_adamw_plan: null pointer in tensor %d", i);
+    AdamEntry& e = entries[i];
+    std::memset(&e, 0, sizeof(e));
+    e.p = t.param;
+    e.g = t.grad;
+    e.m = t.exp_avg;
+    e.v = t.exp_avg_sq;
+    e.numel = t.numel;
+    e.tile_begin = tiles;
+    e.vec = aligned16(t.param) && aligned16(t.grad) && aligned16(t.exp_avg) && aligned16(t.exp_avg_sq);
+    tiles += (t.numel + ADAM_TILE - 1) / ADAM_TILE;
+  }
+  if (tiles > INT32_MAX) return fail(MAD_ERR_INVALID, "mad_adamw_plan: too many tiles");
+  const int64_t need = table_layout(n_tensors, tiles);
+  if (table_bytes < need) return fail(MAD_ERR_WORKSPACE, "mad_adamw_plan: table needs %lld bytes, got %lld",
+                                      static_cast<long long>(need), static_cast<long long>(table_bytes));
+  *n_tiles_out = tiles;
+  if (need == 0) return MAD_OK;
+  std::vector<uint8_t> host(need, 0);
+  std::memcpy(host.data() + entries_offset(tiles), entries.data(), entries.size() * sizeof(AdamEntry));
+  int32_t* map = reinterpret_cast<int32_t*>(host.data());
+  for (int32_t i = 0; i < n_tensors; ++i) {
+    const int64_t nt = (entries[i].numel + ADAM_TILE - 1) / ADAM_TILE;
+    for (int64_t k = 0; k < nt; ++k) map[entries[i].tile_begin + k] = i;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(dev_table, host.data(), need, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return fail_cuda("mad_adamw_plan: table upload");
+  return MAD_OK;
+}
+
+extern "C" int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2,
+                                    float eps, float weight_decay, float bias1, float bias2, void* stream) {
+  clear_error();
+  if (n_tiles < 0) return fail(MAD_ERR_INVALID, "mad_adamw_step_multi: negative tile count");
+  if (n_tiles == 0) return MAD_OK;
+  if (!dev_table) return fail(MAD_ERR_INVALID, "mad_adamw_step_multi: null table");
+  if (!(bias1 > 0.f) || !(bias2 > 0.f))
+    return fail(MAD_ERR_INVALID, "mad_adamw_step_multi: bias corrections must be > 0");
+  const uint8_t* base = static_cast<const uint8_t*>(dev_table);
+  const int32_t* tile_map = reinterpret_cast<const int32_t*>(base);
+  const AdamEntry* entries = reinterpret_cast<const AdamEntry*>(base + entries_offset(n_tiles));
+  adamw_multi_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      entries, tile_map, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
+  return check_launch("adamw_multi_kernel");
+}

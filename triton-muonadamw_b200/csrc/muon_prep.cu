@@ -1,0 +1,186 @@
+// Muon prologue, one pass over every planned matrix (triton_muon.py:346-356):
+//   mom = beta*mom + (1-beta)*g              (buffer updated in place, fp32)
+//   u   = g + beta*(mom - g)  if nesterov    (the buffer itself is untouched)
+//   X   = bf16(u), transposed when rows > cols, so X is m x n with m <= n
+//   s   = 1 / max(bf16(||X||_F), bf16(eps))  (the reference's bf16 norm)
+// X is written unnormalised; s is folded into the first Gram and update
+// epilogues.  The norm is reduced deterministically: every 64x64 tile writes
+// its partial sum of squares, and the last tile of a matrix to finish (found
+// with a per-matrix arrival counter, which it resets) adds the partials in a
+// fixed order in double precision.
+//
+// Traffic per element: read g, mom (8 B), write mom (4 B) and X (2 B).
+#include <cuda_runtime.h>
+
+#include "capi_common.h"
+#include "plan.cuh"
+#include "ptx_sm100.cuh"
+
+namespace mad {
+
+constexpr int PREP_THREADS = 256;
+
+struct PrepScalars {
+  float beta, one_m_beta, eps_bf16;
+  int nesterov;
+};
+
+__device__ __forceinline__ float prep_update(float g, float& mom, const PrepScalars& s) {
+  mom = __fadd_rn(__fmul_rn(mom, s.beta), __fmul_rn(g, s.one_m_beta));
+  return s.nesterov ? __fadd_rn(g, __fmul_rn(s.beta, __fsub_rn(mom, g))) : mom;
+}
+
+__global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __restrict__ mats,
+                                                                 const int32_t* __restrict__ prep_map,
+                                                                 float* __restrict__ partials, int64_t n_tiles,
+                                                                 PrepScalars s) {
+  __shared__ float tile_t[PREP_TILE][PREP_TILE + 1];
+  __shared__ double red[PREP_THREADS / 32];
+  __shared__ int is_last;
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+
+  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int mi = prep_map[tile];
+    MatDesc* md = mats + mi;
+    const int rows = md->rows, cols = md->cols, ld_x = md->ld_x;
+    const int transposed = md->transposed;
+    const int local = static_cast<int>(tile - md->prep_begin);
+    const int r0 = (local / md->prep_tiles_c) * PREP_TILE;
+    const int c0 = (local % md->prep_tiles_c) * PREP_TILE;
+    const float* __restrict__ g = md->g;
+    float* __restrict__ mom = md->mom;
+    __nv_bfloat16* __restrict__ x = md->x[0];
+    const bool full = md->vec != 0 && r0 + PREP_TILE <= rows && c0 + PREP_TILE <= cols;
+
+    float ss = 0.f;
+    const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rl = i * 16 + (t >> 4);
+      const int r = r0 + rl, c = c0 + cl;
+      float xv[4];
+      if (full) {
+        const int64_t off = static_cast<int64_t>(r) * cols + c;
+        const float4 gv = __ldcs(reinterpret_cast<const float4*>(g + off));
+        float4 mv = *reinterpret_cast<const float4*>(mom + off);
+        xv[0] = prep_update(gv.x, mv.x, s);
+        xv[1] = prep_update(gv.y, mv.y, s);
+        xv[2] = prep_update(gv.z, mv.z, s);
+        xv[3] = prep_update(gv.w, mv.w, s);
+        *reinterpret_cast<float4*>(mom + off) = mv;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          xv[k] = 0.f;
+          if (r < rows && c + k < cols) {
+            const int64_t off = static_cast<int64_t>(r) * cols + c + k;
+            float mv = mom[off];
+            xv[k] = prep_update(g[off], mv, s);
+            mom[off] = mv;
+          }
+        }
+      }
+      __nv_bfloat16 xb[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        xb[k] = __float2bfloat16_rn(xv[k]);
+        const float q = __bfloat162float(xb[k]);
+        ss = fmaf(q, q, ss);
+      }
+      if (!transposed) {
+        if (r < rows) {
+          __nv_bfloat16* dst = x + static_cast<int64_t>(r) * ld_x + c;
+          if (c + 4 <= cols) {
+            uint2 packed;
+            packed.x = static_cast<uint32_t>(__bfloat16_as_ushort(xb[0])) |
+                       (static_cast<uint32_t>(__bfloat16_as_ushort(xb[1])) << 16);
+            packed.y = static_cast<uint32_t>(__bfloat16_as_ushort(xb[2])) |
+                       (static_cast<uint32_t>(__bfloat16_as_ushort(xb[3])) << 16);
+            *reinterpret_cast<uint2*>(dst) = packed;
+          } else {
+            for (int k = 0; k < 4 && c + k < cols; ++k) dst[k] = xb[k];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tile_t[cl + k][rl] = __bfloat162float(xb[k]);
+      }
+    }
+
+    if (transposed) {
+      __syncthreads();
+      // X row = parameter column, X column = parameter row.
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int xr = i * 16 + (t >> 4);
+        const int xc = (t & 15) * 4;
+        const int row = c0 + xr, col = r0 + xc;
+        if (row < cols) {
+          __nv_bfloat16* dst = x + static_cast<int64_t>(row) * ld_x + col;
+          if (col + 4 <= rows) {
+            uint2 packed;
+            packed.x = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(tile_t[xr][xc + 0]))) |
+                       (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(tile_t[xr][xc + 1]))) << 16);
+            packed.y = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(tile_t[xr][xc + 2]))) |
+                       (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(tile_t[xr][xc + 3]))) << 16);
+            *reinterpret_cast<uint2*>(dst) = packed;
+          } else {
+            for (int k = 0; k < 4 && col + k < rows; ++k) dst[k] = __float2bfloat16_rn(tile_t[xr][xc + k]);
+          }
+        }
+      }
+    }
+
+    // Block sum of squares -> this tile's partial.
+    float w = ss;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (lane == 0) red[warp] = w;
+    __syncthreads();
+    if (t == 0) {
+      float tot = 0.f;
+      for (int k = 0; k < PREP_THREADS / 32; ++k) tot += static_cast<float>(red[k]);
+      partials[tile] = tot;
+      __threadfence();
+      const unsigned prev = atomicAdd(&md->done, 1u);
+      is_last = (prev == static_cast<unsigned>(md->prep_count) - 1u);
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      double acc = 0.0;
+      const int begin = md->prep_begin, count = md->prep_count;
+      for (int k = t; k < count; k += PREP_THREADS) acc += static_cast<double>(__ldcg(partials + begin + k));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) red[warp] = acc;
+      __syncthreads();
+      if (t == 0) {
+        double tot = 0.0;
+        for (int k = 0; k < PREP_THREADS / 32; ++k) tot += red[k];
+        float norm = bf16_round(static_cast<float>(sqrt(tot)));
+        if (!(norm >= s.eps_bf16)) norm = (norm != norm) ? norm : s.eps_bf16;  // clamp(min=eps), NaN kept
+        md->inv_norm = 1.0f / norm;
+        md->done = 0u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, float beta,
+                     int nesterov, float eps, cudaStream_t stream) {
+  if (n_tiles <= 0) return MAD_OK;
+  PrepScalars s;
+  s.beta = beta;
+  s.one_m_beta = static_cast<float>(1.0 - static_cast<double>(beta));
+  s.eps_bf16 = bf16_round(eps);
+  s.nesterov = nesterov ? 1 : 0;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  const int grid = static_cast<int>(n_tiles < cap ? n_tiles : cap);
+  muon_prep_kernel<<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
+  return check_launch("muon_prep_kernel");
+}
+
+}  // namespace mad

@@ -1,0 +1,82 @@
+// Device-side plan tables shared by the host planner and the kernels.
+//
+// A Muon plan is one contiguous device buffer (the "table") holding, in order:
+//   PlanHeader | MatDesc[n] | CUtensorMap[6n] | TileRef lists (gram, poly,
+//   update) | prep tile -> matrix map | prep partial sums
+// plus a second buffer (the "work") with each matrix's bf16 Newton-Schulz
+// operands: two X buffers (ping-pong), the Gram matrix A and the polynomial B.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+namespace mad {
+
+// ---------------------------------------------------------------- AdamW
+// One tensor of the multi-tensor AdamW launch.  `vec` is 1 when all four
+// pointers are 16-byte aligned, so whole float4 loads/stores are legal.
+struct AdamEntry {
+  float* p;
+  const float* g;
+  float* m;
+  float* v;
+  int64_t numel;
+  int64_t tile_begin;  // first global tile index of this tensor
+  int32_t vec;
+  int32_t pad;
+};
+static_assert(sizeof(AdamEntry) == 56, "AdamEntry layout");
+
+constexpr int ADAM_THREADS = 256;
+constexpr int ADAM_TILE = 4096;  // elements per tile: 256 threads x 4 float4
+
+// ---------------------------------------------------------------- Muon
+constexpr int TM_XK0 = 0;   // X ping buffer, K-major box {64, 128}
+constexpr int TM_XK1 = 1;   // X pong buffer, K-major box {64, 128}
+constexpr int TM_XMN0 = 2;  // X ping buffer, MN-major box {64, 64}
+constexpr int TM_XMN1 = 3;  // X pong buffer, MN-major box {64, 64}
+constexpr int TM_GRAM = 4;  // A = X Xᵀ, K-major box {64, 128}
+constexpr int TM_POLY = 5;  // B = bA + cA², K-major box {64, 128}
+constexpr int TMAPS_PER_MAT = 6;
+
+constexpr int PREP_TILE = 64;  // prep works on 64x64 tiles of the parameter
+
+struct MatDesc {
+  float* p;              // parameter, rows x cols, row-major fp32
+  const float* g;        // gradient, same layout
+  float* mom;            // momentum buffer, same layout
+  __nv_bfloat16* x[2];   // Newton-Schulz iterate, m x n (ld_x), ping-pong
+  __nv_bfloat16* gram;   // A, m x m (ld_mm)
+  __nv_bfloat16* poly;   // B, m x m (ld_mm)
+  double lr_scale;       // shape factor: scaled_lr = float(lr * lr_scale)
+  int32_t rows, cols;    // parameter shape
+  int32_t m, n;          // wide shape: m = min(rows, cols), n = max(rows, cols)
+  int32_t ld_x, ld_mm;   // leading dimensions (elements), multiples of 64
+  int32_t transposed;    // rows > cols: X = uᵀ
+  float inv_norm;        // 1 / max(bf16(||X||_F), bf16(eps)), written by prep
+  int32_t prep_begin;    // first prep tile of this matrix
+  int32_t prep_tiles_c;  // prep tiles along cols
+  int32_t prep_count;    // number of prep tiles
+  uint32_t done;         // prep tiles finished this step (reset by the last one)
+  int32_t tmap_base;     // index of this matrix's first tensor map
+  int32_t vec;           // p, g, mom 16-byte aligned and cols % 4 == 0
+  int32_t pad[2];
+};
+static_assert(sizeof(MatDesc) == 128, "MatDesc layout");
+
+struct TileRef {
+  int32_t mat;
+  int32_t tm;  // row block (128 rows)
+  int32_t tn;  // column block (256 columns)
+  int32_t pad;
+};
+
+struct PlanHeader {
+  uint32_t status;   // device error bits, sticky until the host clears them
+  int32_t n_mats;
+  int32_t pad[62];
+};
+static_assert(sizeof(PlanHeader) == 256, "PlanHeader size");
+
+}  // namespace mad

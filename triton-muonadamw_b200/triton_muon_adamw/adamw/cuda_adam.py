@@ -1,0 +1,127 @@
+"""AdamW branch of MuonAdamW on the B200: one multi-tensor CUDA launch per step.
+
+Replaces the reference's ``TritonAdamW`` (triton_adam.py:106-161), keeping
+its name, constructor, attributes (``model_params``, ``m``, ``v``,
+``step_num``, ``lr``, ``beta1``, ``beta2``, ``weight_decay``, ``eps``) and
+behaviour: float32 ``exp_avg``/``exp_avg_sq`` allocated at construction, one
+branch-global step count for the bias corrections, parameters whose ``grad``
+is ``None`` skipped, ``zero_grad`` zeroing gradients in place.
+
+Where the reference launches one Triton kernel per tensor, ``step()`` launches
+one kernel for all tensors (``mad_adamw_step_multi``), driven by a tile table
+that is rebuilt only when a tensor's storage changes.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Iterable
+
+import torch
+import torch.nn as nn
+
+from .. import _lib
+
+
+def _check_tensor(p: torch.Tensor, what: str) -> None:
+    if not p.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor (this optimizer runs only on the GPU)")
+    if p.dtype != torch.float32:
+        raise TypeError(f"{what} must be float32, got {p.dtype}")
+    if not p.is_contiguous():
+        raise ValueError(f"{what} must be contiguous")
+
+
+class AdamWTable:
+    """Device tile table over a list of (param, grad, exp_avg, exp_avg_sq) float32 views."""
+
+    def __init__(self):
+        self.key = None
+        self.table = None
+        self.n_tiles = 0
+        self.numel = 0
+
+    def ensure(self, quads, device) -> None:
+        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel()) for p, g, m, v in quads)
+        if key == self.key:
+            return
+        lib = _lib.load()
+        arr = (_lib.AdamWTensor * max(1, len(quads)))()
+        for i, (p, g, m, v) in enumerate(quads):
+            arr[i] = _lib.AdamWTensor(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel())
+        nbytes = ctypes.c_int64()
+        _lib.check(lib.mad_adamw_table_bytes(arr, len(quads), ctypes.byref(nbytes)), "mad_adamw_table_bytes")
+        self.table = torch.empty(max(1, nbytes.value), dtype=torch.uint8, device=device)
+        n_tiles = ctypes.c_int64()
+        _lib.check(lib.mad_adamw_plan(arr, len(quads), self.table.data_ptr(), nbytes.value, ctypes.byref(n_tiles),
+                                      _lib.stream_handle()), "mad_adamw_plan")
+        self.n_tiles = n_tiles.value
+        self.numel = sum(p.numel() for p, _, _, _ in quads)
+        self.key = key
+
+    def launch(self, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2) -> None:
+        if self.n_tiles == 0:
+            return
+        lib = _lib.load()
+        _lib.check(lib.mad_adamw_step_multi(self.table.data_ptr(), self.n_tiles, lr, beta1, beta2, eps, weight_decay,
+                                            bias1, bias2, _lib.stream_handle()), "mad_adamw_step_multi")
+
+
+class TritonAdamW:
+    """AdamW over float32 CUDA parameters, one CUDA launch per step.
+
+    The name is the reference's (``triton_muon_adamw.adamw.TritonAdamW``) so
+    imports keep working; there is no Triton code behind it.
+    """
+
+    def __init__(
+        self,
+        params: Iterable[nn.Parameter] | list[nn.Parameter],
+        lr=1e-3,
+        betas: tuple[float, float] = (0.9, 0.999),
+        weight_decay=1e-2,
+        eps=1e-7,
+    ):
+        self.model_params = list(params)
+        self.beta1 = betas[0]
+        self.beta2 = betas[1]
+        self.lr = lr
+        self.weight_decay = weight_decay
+        self.eps = eps
+        self.step_num = 0
+        self.m = {}
+        self.v = {}
+        for param in self.model_params:
+            self.m[param] = torch.zeros_like(param, dtype=torch.float32)
+            self.v[param] = torch.zeros_like(param, dtype=torch.float32)
+        self._table = AdamWTable()
+
+    def _active(self):
+        quads = []
+        for p in self.model_params:
+            if p.grad is None:
+                continue
+            _check_tensor(p, "AdamW parameter")
+            _check_tensor(p.grad, "AdamW gradient")
+            quads.append((p.data, p.grad, self.m[p], self.v[p]))
+        return quads
+
+    @torch.no_grad()
+    def step(self):
+        """One AdamW update of every parameter that has a gradient (triton_adam.py:132-153)."""
+        self.step_num += 1
+        quads = self._active()
+        if not quads:
+            return
+        self._table.ensure(quads, quads[0][0].device)
+        if getattr(self, "_timer", None) is not None:
+            self._timer.mark("adamw")
+        self._table.launch(lr=self.lr, beta1=self.beta1, beta2=self.beta2, eps=self.eps,
+                           weight_decay=self.weight_decay, bias1=1 - self.beta1 ** self.step_num,
+                           bias2=1 - self.beta2 ** self.step_num)
+
+    def zero_grad(self):
+        """Reset gradients to zero in place (triton_adam.py:155-161)."""
+        for param in self.model_params:
+            if param.grad is not None:
+                param.grad.zero_()

@@ -1,0 +1,251 @@
+"""Hybrid MuonAdamW optimizer: drop-in replacement of the reference's API.
+
+Same public surface as the reference's ``triton_muon_adamw/optimizer.py``:
+``AdamConfig`` and ``MuonConfig`` (field names, types and defaults,
+optimizer.py:14-67), ``MuonAdamW`` (constructor, auto/explicit parameter
+routing, ``step``/``zero_grad``/``state_dict``/``load_state_dict``,
+attributes ``adamw``/``muon``/``param_group``; optimizer.py:70-175) and
+``PyTorchMuonAdamW``, the ``torch.optim`` comparison wrapper
+(optimizer.py:178-260).
+
+``MuonAdamW.step()`` runs the AdamW branch (one CUDA launch) and then the
+Muon branch (2 + 3*ns_steps CUDA launches) on the current CUDA stream.  Given
+a ``torch.distributed`` process group of size > 1 it shards the work: whole
+Muon matrices per rank (size-balanced) and ZeRO-1 AdamW element ranges,
+followed by an NCCL all-gather of the updated parameters.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Literal, TypeAlias
+
+import torch
+import torch.nn as nn
+
+from .adamw.cuda_adam import TritonAdamW
+from .muon.cuda_muon import TritonMuon
+
+ParameterGroups: TypeAlias = dict[str, list[nn.Parameter]]
+
+
+@dataclass
+class AdamConfig:
+    """Hyperparameters for the AdamW branch of :class:`MuonAdamW`.
+
+    Parameters
+    ----------
+    lr:
+        Learning rate used by AdamW.
+    betas:
+        Coefficients of the first- and second-moment running averages.
+    eps:
+        Term added to the denominator for numerical stability.
+    weight_decay:
+        Decoupled AdamW weight decay coefficient.
+    """
+
+    lr: float = 1e-3
+    betas: tuple[float, float] = (0.9, 0.999)
+    eps: float = 1e-7
+    weight_decay: float = 0.01
+
+
+@dataclass
+class MuonConfig:
+    """Hyperparameters for the Muon branch of :class:`MuonAdamW`.
+
+    Parameters
+    ----------
+    lr:
+        Learning rate used by Muon.
+    beta:
+        Momentum coefficient.
+    eps:
+        Lower bound of the Frobenius norm used to normalise the update.
+    weight_decay:
+        Decoupled weight decay coefficient.
+    coeffs:
+        Coefficients (a, b, c) of the Newton-Schulz polynomial.
+    nesterov:
+        Whether to use Nesterov momentum.
+    ns_steps:
+        Number of Newton-Schulz iterations.
+    adjust_lr_fn:
+        Shape-dependent learning-rate adjustment of the Muon update.
+    """
+
+    lr: float = 1e-3
+    beta: float = 0.95
+    eps: float = 1e-7
+    weight_decay: float = 0.1
+    coeffs: tuple[float, float, float] = (3.445, -4.775, 2.0315)
+    nesterov: bool = True
+    ns_steps: int = 5
+    adjust_lr_fn: Literal["original", "match_rms_adamw", "spectral_unclamped"] = "original"
+
+
+def split_parameters(model_params, parameter_split):
+    """Route parameters to AdamW or Muon exactly as the reference does (optimizer.py:107-130).
+
+    ``explicit``: the ``"adam"``/``"muon"`` lists of a dict.  ``auto``: every
+    trainable 2-D parameter except the input embedding and the output head
+    goes to Muon, everything else to AdamW; parameters sharing storage (a
+    tied head) are taken once.
+    """
+    adam_params, muon_params = [], []
+    if parameter_split == "explicit" and not isinstance(model_params, dict):
+        raise ValueError("When parameter_split is 'explicit', params must be a dictionary with keys 'adam' and "
+                         "'muon' and their corresponding parameters.")
+    if parameter_split == "auto" and isinstance(model_params, dict):
+        raise ValueError("When parameter_split is 'auto', params must be an nn.Module (ie the model itself), not a "
+                         "dictionary.")
+    if parameter_split == "explicit":
+        adam_params = list(model_params.get("adam", []))
+        muon_params = list(model_params.get("muon", []))
+    elif parameter_split == "auto":
+        embed = model_params.get_input_embeddings().weight
+        out = model_params.get_output_embeddings()
+        head = out.weight if out is not None else None
+        seen_ptrs = set()
+        for p in model_params.parameters():
+            if not p.requires_grad or p.data_ptr() in seen_ptrs:
+                continue
+            seen_ptrs.add(p.data_ptr())
+            if p.ndim == 2 and p is not embed and p is not head:
+                muon_params.append(p)
+            else:
+                adam_params.append(p)
+    return adam_params, muon_params
+
+
+class MuonAdamW(TritonMuon, TritonAdamW):
+    """Optimizer that routes parameters to Muon or AdamW and updates them on the GPU.
+
+    Two-dimensional parameters are updated with Muon, except the input
+    embedding and the output head; all other trainable parameters (biases,
+    norms, embeddings, heads) use AdamW.  Parameters must be float32,
+    contiguous CUDA tensors; there is no CPU implementation.
+
+    Parameters
+    ----------
+    model_params:
+        The model (``parameter_split="auto"``) or a dict with ``"adam"`` and
+        ``"muon"`` parameter lists (``"explicit"``).  In auto mode the model
+        must provide ``get_input_embeddings()`` and ``get_output_embeddings()``.
+    muon_config, adam_config:
+        Hyperparameters of the two branches.
+    parameter_split:
+        ``"auto"`` or ``"explicit"``.
+    process_group:
+        Optional ``torch.distributed`` process group (NCCL).  With more than
+        one rank, Muon matrices are owned whole by one rank each, AdamW state
+        is sharded ZeRO-1 style, and the updated parameters are all-gathered.
+        Gradients are expected to be identical on every rank already.
+    """
+
+    def __init__(
+        self,
+        model_params: nn.Module | ParameterGroups,
+        muon_config: MuonConfig = MuonConfig(),  # noqa: B008
+        adam_config: AdamConfig = AdamConfig(),  # noqa: B008
+        parameter_split: Literal["auto", "explicit"] = "auto",
+        process_group=None,
+    ) -> None:
+        adam_params, muon_params = split_parameters(model_params, parameter_split)
+        self.process_group = process_group
+        self.distributed = None
+        if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
+            from .distributed import ShardedMuonAdamW  # noqa: PLC0415
+            self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group)
+            self.adamw = self.distributed.adamw
+            self.muon = self.distributed.muon
+        else:
+            self.adamw = TritonAdamW(params=adam_params, lr=adam_config.lr, betas=adam_config.betas,
+                                     weight_decay=adam_config.weight_decay, eps=adam_config.eps)
+            self.muon = TritonMuon(params=muon_params, lr=muon_config.lr, beta=muon_config.beta,
+                                   eps=muon_config.eps, weight_decay=muon_config.weight_decay,
+                                   coeffs=muon_config.coeffs, nesterov=muon_config.nesterov,
+                                   ns_steps=muon_config.ns_steps, adjust_lr_fn=muon_config.adjust_lr_fn)
+        self.param_group = {
+            "adam": self.adamw.model_params,
+            "muon": self.muon.model_params,
+        }
+
+    def step(self) -> None:
+        """Apply one update with both branches: AdamW, then Muon (optimizer.py:156-159)."""
+        if self.distributed is not None:
+            self.distributed.step()
+            return
+        self.adamw.step()
+        self.muon.step()
+
+    def zero_grad(self) -> None:
+        """Reset the gradients of both branches to zero in place."""
+        self.adamw.zero_grad()
+        self.muon.zero_grad()
+
+    def device_status(self, clear: bool = True) -> int:
+        """Error bits recorded by the Muon kernels since the last read (0 = healthy)."""
+        return self.muon.device_status(clear)
+
+    # -- checkpointing -----------------------------------------------------
+    def state_dict(self) -> dict[str, object]:
+        """Optimizer state in the layout of ``PyTorchMuonAdamW.state_dict()``.
+
+        ``{"adam": <torch.optim.AdamW state dict>, "muon": <torch.optim.Muon
+        state dict>}``: per-parameter ``step``/``exp_avg``/``exp_avg_sq`` and
+        ``momentum_buffer``, indexed by position in each branch's parameter
+        list, so checkpoints move between the two classes.  (The reference's
+        own ``state_dict`` returns only the parameter lists, optimizer.py:166-168.)
+        """
+        from .checkpoint import branch_state_dicts  # noqa: PLC0415
+        return branch_state_dicts(self)
+
+    def load_state_dict(self, state_dict: dict[str, object]) -> None:
+        """Load a dict produced by :meth:`state_dict` or by ``PyTorchMuonAdamW.state_dict()``."""
+        from .checkpoint import load_branch_state_dicts  # noqa: PLC0415
+        load_branch_state_dicts(self, state_dict)
+
+
+class PyTorchMuonAdamW:
+    """``torch.optim`` comparison optimizer with the same routing and configs.
+
+    Delegates to ``torch.optim.AdamW(fused=True)`` and ``torch.optim.Muon``
+    exactly as the reference's wrapper does (optimizer.py:178-260), including
+    passing neither ``coeffs`` nor ``eps`` to ``torch.optim.Muon`` (which then
+    uses its own defaults).  It is for comparisons; :class:`MuonAdamW` never
+    uses it.
+    """
+
+    def __init__(
+        self,
+        model_params: nn.Module | ParameterGroups,
+        muon_config: MuonConfig = MuonConfig(),  # noqa: B008
+        adam_config: AdamConfig = AdamConfig(),  # noqa: B008
+        parameter_split: Literal["auto", "explicit"] = "auto",
+    ) -> None:
+        adam_params, muon_params = split_parameters(model_params, parameter_split)
+        self.adamw = torch.optim.AdamW(params=adam_params, lr=adam_config.lr, betas=adam_config.betas,
+                                       weight_decay=adam_config.weight_decay, eps=adam_config.eps, fused=True)
+        self.muon = torch.optim.Muon(params=muon_params, lr=muon_config.lr, momentum=muon_config.beta,
+                                     weight_decay=muon_config.weight_decay, nesterov=muon_config.nesterov,
+                                     ns_steps=muon_config.ns_steps, adjust_lr_fn=muon_config.adjust_lr_fn)
+
+    def step(self) -> None:
+        """One ``torch.optim`` AdamW update, then one Muon update."""
+        self.adamw.step()
+        self.muon.step()
+
+    def zero_grad(self) -> None:
+        self.adamw.zero_grad()
+        self.muon.zero_grad()
+
+    def state_dict(self) -> dict[str, object]:
+        return {"adam": self.adamw.state_dict(), "muon": self.muon.state_dict()}
+
+    def load_state_dict(self, state_dict: dict[str, object]) -> None:
+        if "adam" in state_dict:
+            self.adamw.load_state_dict(state_dict["adam"])
+        if "muon" in state_dict:
+            self.muon.load_state_dict(state_dict["muon"])
