@@ -133,7 +133,7 @@ int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* dev_table, 
 
 /* Momentum EMA, Nesterov, bf16 cast, transpose-to-wide and the Frobenius
  * norm of every planned matrix, in one launch. */
-int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, float beta, int32_t nesterov, float eps,
+int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float eps,
                   void* stream);
 
 /* Newton-Schulz iteration `iter` (0-based), one launch each:
@@ -150,7 +150,7 @@ int mad_ns_update(const mad_muon_plan_info* info, void* dev_table, int32_t iter,
 
 /* The whole Muon branch for every planned matrix: prep, then ns_steps x
  * (gram, poly, update), the last update writing the parameters. */
-int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, float beta, int32_t nesterov, float a,
+int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float a,
                         float b, float c, int32_t ns_steps, float eps, double lr, double weight_decay, void* stream);
 
 /* Copies the plan's device status word to *status (synchronises `stream`)

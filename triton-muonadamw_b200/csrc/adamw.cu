@@ -113,15 +113,18 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_single_kernel(AdamEntry e,
   }
 }
 
+// The reference kernel receives its scalars as float32 and forms 1-beta1,
+// 1-beta2 and 1-lr*wd in float32 (triton_adam.py:53-58); so do we.
 static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, float wd, float bias1, float bias2) {
   AdamScalars s;
+  volatile float lr_wd = lr * wd;  // one float32 rounding, never contracted into the subtraction
   s.lr = lr;
   s.beta1 = beta1;
   s.beta2 = beta2;
-  s.one_m_beta1 = static_cast<float>(1.0 - static_cast<double>(beta1));
-  s.one_m_beta2 = static_cast<float>(1.0 - static_cast<double>(beta2));
+  s.one_m_beta1 = 1.0f - beta1;
+  s.one_m_beta2 = 1.0f - beta2;
   s.eps = eps;
-  s.decay = static_cast<float>(1.0 - static_cast<double>(lr) * static_cast<double>(wd));
+  s.decay = 1.0f - lr_wd;
   s.bias1 = bias1;
   s.bias2 = bias2;
   return s;

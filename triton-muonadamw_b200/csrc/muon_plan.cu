@@ -21,7 +21,7 @@
 
 namespace mad {
 
-int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, float beta,
+int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, double beta,
                      int nesterov, float eps, cudaStream_t stream);
 int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, const TileRef* tiles, int64_t n_tiles,
                    int iter, int last, float a, float b, float c, double lr, float lr_wd, unsigned int* status,
@@ -312,7 +312,7 @@ int check_args(const mad_muon_plan_info* info, void* table, const char* who) {
 
 }  // namespace
 
-extern "C" int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, float beta, int32_t nesterov,
+extern "C" int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
                              float eps, void* stream) {
   clear_error();
   if (int rc = check_args(info, dev_table, "mad_muon_prep")) return rc;
@@ -357,7 +357,7 @@ extern "C" int mad_ns_update(const mad_muon_plan_info* info, void* dev_table, in
                         v.status, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, float beta, int32_t nesterov,
+extern "C" int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
                                    float a, float b, float c, int32_t ns_steps, float eps, double lr,
                                    double weight_decay, void* stream) {
   clear_error();

@@ -25,8 +25,10 @@ struct PrepScalars {
   int nesterov;
 };
 
+// mom.mul_(beta).add_(grad, alpha=1-beta) (triton_muon.py:346): one rounded
+// product, then torch's fused `self + alpha*other` (a single FMA rounding).
 __device__ __forceinline__ float prep_update(float g, float& mom, const PrepScalars& s) {
-  mom = __fadd_rn(__fmul_rn(mom, s.beta), __fmul_rn(g, s.one_m_beta));
+  mom = __fmaf_rn(s.one_m_beta, g, __fmul_rn(mom, s.beta));
   return s.nesterov ? __fadd_rn(g, __fmul_rn(s.beta, __fsub_rn(mom, g))) : mom;
 }
 
@@ -169,12 +171,14 @@ __global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __rest
   }
 }
 
-int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, float beta,
+int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, double beta,
                      int nesterov, float eps, cudaStream_t stream) {
   if (n_tiles <= 0) return MAD_OK;
   PrepScalars s;
-  s.beta = beta;
-  s.one_m_beta = static_cast<float>(1.0 - static_cast<double>(beta));
+  // The reference passes Python floats: beta is rounded to float32 by the
+  // multiply, alpha = 1 - beta is formed in double and then rounded.
+  s.beta = static_cast<float>(beta);
+  s.one_m_beta = static_cast<float>(1.0 - beta);
   s.eps_bf16 = bf16_round(eps);
   s.nesterov = nesterov ? 1 : 0;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 8;

@@ -57,12 +57,13 @@ SIGNATURES = {
     "mad_muon_plan_size": (ctypes.c_int, [ctypes.POINTER(MuonMatrix), c_int32, ctypes.POINTER(MuonPlanInfo)]),
     "mad_muon_plan": (ctypes.c_int, [ctypes.POINTER(MuonMatrix), c_int32, c_void_p, c_void_p,
                                      ctypes.POINTER(MuonPlanInfo), ctypes.POINTER(MuonBuffers), c_void_p]),
-    "mad_muon_prep": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_float, c_int32, c_float, c_void_p]),
+    "mad_muon_prep": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32, c_float,
+                                     c_void_p]),
     "mad_ns_gram": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_int32, c_void_p]),
     "mad_ns_poly": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_int32, c_float, c_float, c_void_p]),
     "mad_ns_update": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_int32, c_int32, c_float,
                                      ctypes.c_double, ctypes.c_double, c_void_p]),
-    "mad_muon_step_multi": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_float, c_int32, c_float,
+    "mad_muon_step_multi": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32, c_float,
                                            c_float, c_float, c_int32, c_float, ctypes.c_double, ctypes.c_double,
                                            c_void_p]),
     "mad_muon_read_status": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.POINTER(ctypes.c_uint32),
