@@ -58,11 +58,19 @@ def llama_shapes(d, layers, n_heads, n_kv_heads, ffn, vocab, tied=False):
     return adam, muon
 
 
+def profiling_shapes():
+    """Small case for ncu captures: one matrix of each 8B Muon orientation (about 2 GB on the device)."""
+    return [("embed", (4096, 4096)), ("final_norm", (4096,))], [("wide", (4096, 14336)), ("tall", (14336, 4096)),
+                                                                 ("square", (4096, 4096))]
+
+
 CONFIGS = {
     "8b": dict(name="llama3-8b-shaped", shapes=lambda: llama_shapes(4096, 32, 32, 8, 14336, 128256),
                adam=dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)),
     "1b3": dict(name="llama-1.3b", shapes=lambda: llama_shapes(2048, 24, 16, 16, 5504, 32000),
                 adam=dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)),
+    "prof": dict(name="profiling-case (3 Muon matrices of the 8B shapes)", shapes=profiling_shapes,
+                 adam=dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)),
 }
 
 
@@ -327,6 +335,7 @@ def main():
         gbs = 14.0 * elems_muon / (avg * 1e-3) / 1e9
         kernels["muon_prep"] = {"launches": len(per["prep"]), "avg_ms": round(avg, 4), "gbs": round(gbs, 1),
                                 "frac": round(gbs / hbm, 3), "bytes_per_elem": 14}
+    # per Newton-Schulz iteration (one gram + one poly + one update launch over all matrices)
     ns_ms = sum(sum(per.get(k, [])) for k in ("gram", "poly", "update")) / max(1, len(per.get("update", [1])))
     ns_total = sum(flops.values())
     upd = kernels.get("ns_gemm_update", {})
@@ -336,7 +345,8 @@ def main():
                 "frac": upd.get("frac_sustained"), "peak_kind": f"{peak_src} sustained bf16",
                 "traffic": traffic, "ns_all_tflops": round(ns_total / (ns_ms * 1e-3) / 1e12, 1) if ns_ms else None,
                 "ns_all_frac_sustained": round(ns_total / (ns_ms * 1e-3) / 1e12 / tf_sus, 3) if ns_ms else None,
-                "ns_ms_per_step": round(ns_ms, 3)}
+                "ns_ms_per_step": round(ns_ms * args.ns_steps, 3),
+                "ns_flops_per_step": ns_total * args.ns_steps}
 
     # End to end: this step's gradients from pinned host memory, result read back.
     e2e = run_e2e(opt, model, dev, args, barrier, world)

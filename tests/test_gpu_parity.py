@@ -9,8 +9,10 @@ Tolerances (written per test):
   bf16 once; accumulation order may flip a rounding, so 1 bf16 ulp
   (rtol 2^-7) plus a tiny atol.
 * Full Muon update: against the oracle with the kernels' own rounding
-  points (normalisation folded), 5e-3 relative Frobenius error (2e-2 for
-  matrices with fewer than 16 rows/cols); against the reference's ordering,
+  points (normalisation folded), 1.2e-2 relative Frobenius error (2e-2 for
+  matrices with fewer than 16 rows/cols) -- twice the 0.35-0.6% that fp32
+  instead of fp64 accumulation alone produces through five iterations
+  (bf16 rounding flips amplified by the polynomial); against the reference's ordering,
   where bf16 placement noise adds up to ~2% (measured), 3e-2 (8e-2 tiny);
   parameters with the reference's Muon bar atol/rtol 1e-2.
 """
@@ -216,7 +218,7 @@ def test_muon_update_matches_oracle(cuda_device, shapes, nesterov, ns_steps):
             # only fp32 accumulation order differs.
             o_fold = orthogonalize(u, COEFFS, ns_steps, 1e-7, normalize="fold")
             err = float((o_gpu - o_fold).norm() / o_fold.norm())
-            assert err < (2e-2 if tiny else 5e-3), f"{tuple(p.shape)} step {step}: vs fold {err:.3e}"
+            assert err < (2e-2 if tiny else 1.2e-2), f"{tuple(p.shape)} step {step}: vs fold {err:.3e}"
             # The reference's ordering (X/||X|| rounded to bf16 first): bf16 placement noise on top.
             o_ref = orthogonalize(u, COEFFS, ns_steps, 1e-7)
             err = float((o_gpu - o_ref).norm() / o_ref.norm())
