@@ -7,7 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 
-#include "../../include/muon_adamw_b200.h"
+#include "muon_adamw_b200.h"  // include/ of the repository (-I)
 
 namespace mad {
 

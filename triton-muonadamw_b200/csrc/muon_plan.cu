@@ -83,17 +83,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 matrix rows x cols (leading dimension ld elements), 128-byte swizzled
-// boxes of 64 columns x box_rows rows.
-int encode_bf16(CUtensorMap* out, void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// bf16 matrix rows x cols (leading dimension ld elements), boxes of
+// box_cols x box_rows; box_cols = 64 uses the 128-byte swizzle (operand
+// loads), box_cols = 32 the 64-byte swizzle (epilogue stores).
+int encode_bf16(CUtensorMap* out, void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                int box_cols = 64) {
   auto fn = encode_fn();
   if (!fn) return fail(MAD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapSwizzle sw = box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MAD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %lldx%lld ld %lld box %d", static_cast<int>(r),
@@ -220,6 +223,10 @@ extern "C" int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* 
     if (int rc = encode_bf16(t + TM_XMN1, d.x[1], s.m, s.n, s.ld_x, 64)) return rc;
     if (int rc = encode_bf16(t + TM_GRAM, d.gram, s.m, s.m, s.ld_mm, 128)) return rc;
     if (int rc = encode_bf16(t + TM_POLY, d.poly, s.m, s.m, s.ld_mm, 128)) return rc;
+    if (int rc = encode_bf16(t + TM_GRAM_ST, d.gram, s.m, s.m, s.ld_mm, 32, 32)) return rc;
+    if (int rc = encode_bf16(t + TM_POLY_ST, d.poly, s.m, s.m, s.ld_mm, 32, 32)) return rc;
+    if (int rc = encode_bf16(t + TM_X0_ST, d.x[0], s.m, s.n, s.ld_x, 32, 32)) return rc;
+    if (int rc = encode_bf16(t + TM_X1_ST, d.x[1], s.m, s.n, s.ld_x, 32, 32)) return rc;
     if (buffers) {
       mad_muon_buffers& b = buffers[i];
       b.x[0] = d.x[0];

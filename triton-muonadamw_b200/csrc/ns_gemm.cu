@@ -18,8 +18,8 @@
 // CTA tile 128 x 256, K step 64 (one 128-byte swizzle atom of bf16), 4-stage
 // TMA ring (48 KB/stage), accumulators double-buffered in TMEM (2 x 256 of
 // the 512 columns) so the epilogue of tile i overlaps the MMAs of tile i+1.
-// Warp 0 issues TMA, warp 1 issues tcgen05.mma (one thread), warps 2-5 drain
-// TMEM (one accumulator row per thread).  Operands: X Xᵀ and A A read two
+// Warp 0 issues TMA, warp 1 issues tcgen05.mma (one thread), warps 2-9 drain
+// TMEM (one accumulator row and half the columns per thread).  Operands: X Xᵀ and A A read two
 // K-major tiles; B X reads B K-major and X MN-major (its rows are the K index).
 #include <cuda_runtime.h>
 
@@ -35,11 +35,22 @@ constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int NUM_THREADS = 192;
-constexpr int EPI_THREADS = 128;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;  // ring + barriers + alignment slack
+constexpr int EPI_WARPS = 8;
+constexpr int EPI_THREADS = EPI_WARPS * 32;
+constexpr int NUM_THREADS = 64 + EPI_THREADS;  // producer warp, MMA warp, epilogue warps
+// Each epilogue warp stages its 32x32 output block (and the transposed mirror
+// block) in shared memory for a TMA store: 2 x 2 KB per warp.
+constexpr int STAGE_OUT_BYTES = 4096;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024 + 1024;  // + barriers, alignment
 
-enum Mode { GRAM = 0, POLY = 1, UPDATE = 2 };
+enum Mode { GRAM = 0, POLY = 1, UPDATE = 2, UPDATE_LAST = 3 };
+
+// UPDATE_LAST is the update of the final iteration, which writes the fp32
+// parameters; it is a separate instantiation so the common path can keep two
+// chunks in flight without exceeding the register budget (168 per thread with
+// ten warps).
+template <int MODE>
+__host__ __device__ constexpr bool is_update() { return MODE == UPDATE || MODE == UPDATE_LAST; }
 
 struct GemmArgs {
   const MatDesc* mats;
@@ -47,7 +58,6 @@ struct GemmArgs {
   const TileRef* tiles;
   int n_tiles;
   int iter;
-  int last;
   float a, b, c;
   float lr_wd;
   double lr;
@@ -59,34 +69,6 @@ __device__ __forceinline__ int k_extent(int mode, const MatDesc& md) { return mo
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(lo))) |
          (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(hi))) << 16);
-}
-
-// 32 consecutive bf16 (64 bytes, 16-byte aligned) -> float.
-__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&out)[32]) {
-  const uint4* s4 = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 u = s4[q];
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      out[q * 8 + 2 * k] = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(w[k] & 0xFFFFu)));
-      out[q * 8 + 2 * k + 1] = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(w[k] >> 16)));
-    }
-  }
-}
-
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 u;
-    u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-    u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-    u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-    u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-    d4[q] = u;
-  }
 }
 
 template <int MODE>
@@ -106,7 +88,7 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
       tmA = tmB = maps + (TM_XK0 + cur);
     } else if (MODE == POLY) {
       tmA = tmB = maps + TM_GRAM;
-    } else {
+    } else {  // UPDATE, UPDATE_LAST
       tmA = maps + TM_POLY;
       tmB = maps + (TM_XMN0 + cur);
     }
@@ -123,7 +105,7 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
       uint8_t* sb = sa + A_BYTES;
       mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
       tma_load_2d(sa, tmA, &full[stage], kb * BK, tr.tm * BM);
-      if (MODE == UPDATE) {
+      if (is_update<MODE>()) {
 #pragma unroll
         for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * (64 * BK * 2), tmB, &full[stage], tr.tn * BN + j * 64, kb * BK);
       } else {
@@ -147,7 +129,7 @@ template <int MODE>
 __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                          uint64_t* tfull, uint64_t* tempty, uint64_t* drain, uint32_t tmem_base,
                                          volatile int* abort_flag) {
-  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, MODE == UPDATE);
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, is_update<MODE>());
   int stage = 0, lt = 0;
   uint32_t phase = 0;
   bool ok = true;
@@ -175,7 +157,7 @@ __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, ui
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
         const uint64_t ad = smem_desc_sw128(sa + kk * 32, 16, 1024);
-        const uint64_t bd = (MODE == UPDATE) ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
+        const uint64_t bd = is_update<MODE>() ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
                                              : smem_desc_sw128(sb + kk * 32, 16, 1024);
         tc_mma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
       }
@@ -192,133 +174,232 @@ __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, ui
   mbar_wait(drain, 0u, args.status, DEV_ERR_MBAR_TIMEOUT_DRAIN);
 }
 
+// Global input one epilogue chunk (32 columns of one accumulator row) reads
+// ahead of time: the bf16 row segment of A (POLY) or X (UPDATE).
+struct ChunkIn {
+  uint4 q[4];  // 32 bf16
+};
+
+template <int MODE>
+__device__ __forceinline__ void chunk_prefetch(const GemmArgs& args, const MatDesc& md, int grow, int gcol0,
+                                               ChunkIn& in) {
+  if (MODE == GRAM) return;
+  const __nv_bfloat16* src = (MODE == POLY) ? md.gram : md.x[args.iter & 1];
+  const int ld = (MODE == POLY) ? md.ld_mm : md.ld_x;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(grow) * ld + gcol0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) in.q[q] = s4[q];
+}
+
+__device__ __forceinline__ float bf16_at(const uint4 (&q)[4], int k) {
+  const uint4& u = q[k >> 3];
+  const uint32_t w = ((k >> 1) & 3) == 0 ? u.x : ((k >> 1) & 3) == 1 ? u.y : ((k >> 1) & 3) == 2 ? u.z : u.w;
+  return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>((k & 1) ? (w >> 16) : (w & 0xFFFFu))));
+}
+
+// Shared-memory address of 16-byte unit `j` of row `r` in a 32-row x 64-byte
+// block under the TMA 64-byte swizzle (16-byte units XOR'ed with bits 7-8).
+__device__ __forceinline__ uint32_t sw64_offset(int r, int j) { return r * 64 + 16 * (j ^ ((r >> 1) & 3)); }
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, unsigned short v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
+// Stage this warp's 32x32 bf16 block (lane = row) and, for strictly upper
+// blocks of a symmetric output, its transpose; then one lane stores both with TMA.
+// Elements outside the matrix are clipped by the tensor map.
+__device__ __forceinline__ void stage_and_store(uint8_t* stage, const float (&v)[32], const CUtensorMap* map,
+                                                int x, int y, bool mirror) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) bulk_wait_read_all();  // the previous chunk's stores are done reading the buffer
+  __syncwarp();
+  const uint32_t base = smem_u32(stage);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+    u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    st_shared_v4(base + sw64_offset(lane, j), u);
+  }
+  if (mirror) {
+    // Transposed block: element (row k, column lane).
+    const uint32_t mbase = base + 2048;
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      st_shared_u16(mbase + sw64_offset(k, lane >> 3) + 2 * (lane & 7), __bfloat16_as_ushort(__float2bfloat16_rn(v[k])));
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, stage, x, y);
+    if (mirror) tma_store_2d(map, stage + 2048, y, x);
+    bulk_commit_group();
+  }
+}
+
+template <int MODE>
+__device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc& md, int grow0, int grow, bool row_ok,
+                                             int gcol0, bool mirror, uint32_t (&acc)[32], const ChunkIn& in,
+                                             uint8_t* stage) {
+  float (&v)[32] = reinterpret_cast<float (&)[32]>(acc);
+  const int m = md.m;
+  if (grow0 >= m) return;  // the warp's rows lie past the matrix: nothing to store (warp-uniform)
+  const CUtensorMap* maps = args.tmaps + md.tmap_base;
+  if (MODE == GRAM || MODE == POLY) {
+    if (MODE == GRAM) {
+      const float s2 = (args.iter == 0) ? md.inv_norm * md.inv_norm : 1.0f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] *= s2;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = __fadd_rn(__fmul_rn(args.b, bf16_at(in.q, k)), __fmul_rn(args.c, v[k]));
+    }
+    stage_and_store(stage, v, maps + (MODE == GRAM ? TM_GRAM_ST : TM_POLY_ST), gcol0, grow0, mirror);
+    return;
+  }
+  // UPDATE
+  const float s = (args.iter == 0) ? md.inv_norm : 1.0f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = __fmul_rn(s, __fadd_rn(__fmul_rn(args.a, bf16_at(in.q, k)), v[k]));
+  if (MODE == UPDATE) {
+    stage_and_store(stage, v, maps + (TM_X0_ST + ((args.iter & 1) ^ 1)), gcol0, grow0, false);
+    return;
+  }
+  if (!row_ok) return;
+  // Parameter write, in two halves of 16 columns: within a half all loads are
+  // issued before any store (a store could otherwise alias a later load and
+  // serialise the chunk).
+  // scaled_lr = lr * shape factor, formed in double and rounded once (triton_muon.py:424-431);
+  // p -= (lr*wd)*p ; p -= scaled_lr*o as two float32 subtractions (triton_muon.py:370-372).
+  const float slr = static_cast<float>(args.lr * md.lr_scale), lr_wd = args.lr_wd;
+  const int n = md.n;
+  float* __restrict__ p = md.p;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int c0 = gcol0 + 16 * h;
+    float pv[16];
+    if (!md.transposed) {
+      float* prow = p + static_cast<int64_t>(grow) * n + c0;
+      const bool vec = md.vec && c0 + 16 <= n;
+      if (vec) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 t = reinterpret_cast<const float4*>(prow)[q];
+          pv[4 * q] = t.x;
+          pv[4 * q + 1] = t.y;
+          pv[4 * q + 2] = t.z;
+          pv[4 * q + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) pv[k] = (c0 + k < n) ? prow[k] : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        pv[k] = __fsub_rn(__fsub_rn(pv[k], __fmul_rn(lr_wd, pv[k])), __fmul_rn(slr, bf16_round(v[16 * h + k])));
+      if (vec) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<float4*>(prow)[q] = make_float4(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          if (c0 + k < n) prow[k] = pv[k];
+      }
+    } else {
+      // Parameter is n x m: X'[grow][col] lives at p[col][grow]; per k a warp touches 128 contiguous bytes.
+      float* pcol = p + static_cast<int64_t>(c0) * m + grow;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) pv[k] = (c0 + k < n) ? pcol[k * m] : 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        pv[k] = __fsub_rn(__fsub_rn(pv[k], __fmul_rn(lr_wd, pv[k])), __fmul_rn(slr, bf16_round(v[16 * h + k])));
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (c0 + k < n) pcol[k * m] = pv[k];
+    }
+  }
+}
+
+// Eight epilogue warps: warp w reads TMEM lanes 32*(w%4).. (the hardware
+// rule) and columns [128*half, 128*half+128) of the tile, half = (w-2)/4.
+// The global inputs of the first chunk are fetched before waiting for the
+// accumulator, and each later chunk's inputs and TMEM load are in flight
+// while the previous chunk is finished.
 template <int MODE>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull, uint64_t* tempty,
-                                              uint32_t tmem_base, volatile int* abort_flag) {
+                                              uint32_t tmem_base, uint8_t* stage, volatile int* abort_flag) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad .. 32*quad+31
+  const int quad = warp & 3;
+  const int half = (warp - 2) >> 2;
   const int row_in_tile = quad * 32 + lane;
-  const int cur = args.iter & 1;
   int lt = 0;
   for (int t = blockIdx.x; t < args.n_tiles; t += gridDim.x, ++lt) {
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
-    const int acc = lt & 1;
+    const int acc_buf = lt & 1;
     const uint32_t acc_phase = static_cast<uint32_t>((lt >> 1) & 1);
-    if (!mbar_wait(&tfull[acc], acc_phase, args.status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE) || *abort_flag) {
+    const int grow0 = tr.tm * BM + quad * 32;
+    const int grow = grow0 + lane;
+    const bool row_ok = grow < md.m;
+    const int col0 = tr.tn * BN + half * 128;
+    // Chunks of this warp that exist (warp-uniform): GRAM/POLY skip blocks below the diagonal.
+    const int limit = is_update<MODE>() ? md.n : md.m;
+    const int blk = col0 / BM;
+    int nch = (col0 < limit) ? (limit - col0 + 31) / 32 : 0;
+    if (nch > 4) nch = 4;
+    if (!is_update<MODE>() && blk < tr.tm) nch = 0;
+    const bool mirror = !is_update<MODE>() && blk > tr.tm;
+    // The parameter-writing update keeps one chunk of global inputs in flight, the others two.
+    constexpr bool PREFETCH_NEXT = MODE != UPDATE_LAST;
+
+    if (lane == 0 && MODE != UPDATE_LAST) {
+      const int st = MODE == GRAM ? TM_GRAM_ST : MODE == POLY ? TM_POLY_ST : TM_X0_ST + ((args.iter & 1) ^ 1);
+      tma_acquire_desc(args.tmaps + md.tmap_base + st);
+    }
+    ChunkIn in[2];
+    if (nch > 0 && row_ok) chunk_prefetch<MODE>(args, md, grow, col0, in[0]);
+    if (!mbar_wait(&tfull[acc_buf], acc_phase, args.status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE) || *abort_flag) {
       *abort_flag = 1;
       break;
     }
     tc_fence_after();
-    const int m = md.m;
-    const int grow = tr.tm * BM + row_in_tile;
-    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-
-    if (MODE == GRAM || MODE == POLY) {
-      const float s2 = (MODE == GRAM && args.iter == 0) ? md.inv_norm * md.inv_norm : 1.0f;
-      __nv_bfloat16* out = (MODE == GRAM) ? md.gram : md.poly;
-      const __nv_bfloat16* ain = md.gram;
-      const int ld = md.ld_mm;
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        const int gcol0 = tr.tn * BN + ch * 32;
-        const int jblk = gcol0 / BM;
-        if (jblk < tr.tm || gcol0 >= m) continue;  // below the diagonal, or past the matrix
-        float v[32];
-        tmem_ld_32cols(tbase + ch * 32, v);
-        if (grow < m) {
-          if (MODE == GRAM) {
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                           static_cast<uint32_t>(acc_buf * BN + half * 128);
+    uint32_t acc[2][32];
+    if (nch > 0) {
+      tmem_ld32_issue(tbase, acc[0]);
+      tmem_ld_wait(acc[0]);
+    }
 #pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] *= s2;
-          } else {
-            float av[32];
-            load_bf16x32(ain + static_cast<int64_t>(grow) * ld + gcol0, av);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] = __fadd_rn(__fmul_rn(args.b, av[k]), __fmul_rn(args.c, v[k]));
-          }
-          store_bf16x32(out + static_cast<int64_t>(grow) * ld + gcol0, v);
-          if (jblk > tr.tm) {
-            // Mirror: element (grow, col) also lands at (col, grow).
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const int col = gcol0 + k;
-              if (col < m) out[static_cast<int64_t>(col) * ld + grow] = __float2bfloat16_rn(v[k]);
-            }
-          }
-        }
+    for (int c = 0; c < 4; ++c) {
+      if (c + 1 < nch) {
+        if (PREFETCH_NEXT && row_ok) chunk_prefetch<MODE>(args, md, grow, col0 + 32 * (c + 1), in[(c + 1) & 1]);
+        tmem_ld32_issue(tbase + 32 * (c + 1), acc[(c + 1) & 1]);
       }
-    } else {  // UPDATE
-      const float s = (args.iter == 0) ? md.inv_norm : 1.0f;
-      const int n = md.n, ld = md.ld_x;
-      const __nv_bfloat16* xin = md.x[cur];
-      __nv_bfloat16* xout = md.x[cur ^ 1];
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        const int gcol0 = tr.tn * BN + ch * 32;
-        if (gcol0 >= n) break;
-        float v[32];
-        tmem_ld_32cols(tbase + ch * 32, v);
-        if (grow < m) {
-          float xv[32];
-          load_bf16x32(xin + static_cast<int64_t>(grow) * ld + gcol0, xv);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = __fmul_rn(s, __fadd_rn(__fmul_rn(args.a, xv[k]), v[k]));
-          if (!args.last) {
-            store_bf16x32(xout + static_cast<int64_t>(grow) * ld + gcol0, v);
-          } else {
-            // scaled_lr = lr * shape factor, formed in double and rounded once (triton_muon.py:424-431).
-            const float slr = static_cast<float>(args.lr * md.lr_scale), lr_wd = args.lr_wd;
-            float* __restrict__ p = md.p;
-            if (!md.transposed) {
-              // X' row grow is parameter row grow (parameter is m x n).
-              float* prow = p + static_cast<int64_t>(grow) * n + gcol0;
-              if (md.vec && gcol0 + 32 <= n) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  float4 pv = reinterpret_cast<float4*>(prow)[q];
-                  float* e = reinterpret_cast<float*>(&pv);
-#pragma unroll
-                  for (int k = 0; k < 4; ++k) {
-                    const float o = bf16_round(v[q * 4 + k]);
-                    const float p1 = __fsub_rn(e[k], __fmul_rn(lr_wd, e[k]));
-                    e[k] = __fsub_rn(p1, __fmul_rn(slr, o));
-                  }
-                  reinterpret_cast<float4*>(prow)[q] = pv;
-                }
-              } else {
-                for (int k = 0; k < 32 && gcol0 + k < n; ++k) {
-                  const float o = bf16_round(v[k]);
-                  const float p1 = __fsub_rn(prow[k], __fmul_rn(lr_wd, prow[k]));
-                  prow[k] = __fsub_rn(p1, __fmul_rn(slr, o));
-                }
-              }
-            } else {
-              // Parameter is n x m; X'[grow][col] is p[col][grow]: lanes write consecutive grow.
-#pragma unroll 4
-              for (int k = 0; k < 32; ++k) {
-                const int col = gcol0 + k;
-                if (col < n) {
-                  float* pe = p + static_cast<int64_t>(col) * m + grow;
-                  const float o = bf16_round(v[k]);
-                  const float p1 = __fsub_rn(*pe, __fmul_rn(lr_wd, *pe));
-                  *pe = __fsub_rn(p1, __fmul_rn(slr, o));
-                }
-              }
-            }
-          }
-        }
-      }
+      if (!PREFETCH_NEXT && c > 0 && c < nch && row_ok) chunk_prefetch<MODE>(args, md, grow, col0 + 32 * c, in[c & 1]);
+      if (c < nch)
+        chunk_finish<MODE>(args, md, grow0, grow, row_ok, col0 + 32 * c, mirror, acc[c & 1], in[c & 1], stage);
+      if (c + 1 < nch) tmem_ld_wait(acc[(c + 1) & 1]);
     }
     tc_fence_before();
-    mbar_arrive(&tempty[acc]);
+    mbar_arrive(&tempty[acc_buf]);
   }
+  if (lane == 0) bulk_wait_all();  // every output store has landed before the CTA retires
 }
 
 template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + STAGES * STAGE_BYTES);
+  uint8_t* stage_out = ring + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + EPI_WARPS * STAGE_OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -354,7 +435,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
   } else if (warp == 1) {
     if (lane == 0) mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, abort_flag);
   } else {
-    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, abort_flag);
+    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * STAGE_OUT_BYTES, abort_flag);
   }
   tc_fence_before();
   __syncthreads();
@@ -386,7 +467,6 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
   args.tiles = tiles;
   args.n_tiles = static_cast<int>(n_tiles);
   args.iter = iter;
-  args.last = last;
   args.a = a;
   args.b = b;
   args.c = c;
@@ -399,7 +479,8 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
     case ns::POLY:
       return ns::launch<ns::POLY>(args, stream, "ns_gemm_kernel<POLY>");
     default:
-      return ns::launch<ns::UPDATE>(args, stream, "ns_gemm_kernel<UPDATE>");
+      return last ? ns::launch<ns::UPDATE_LAST>(args, stream, "ns_gemm_kernel<UPDATE_LAST>")
+                  : ns::launch<ns::UPDATE>(args, stream, "ns_gemm_kernel<UPDATE>");
   }
 }
 

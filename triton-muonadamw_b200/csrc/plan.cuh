@@ -38,7 +38,12 @@ constexpr int TM_XMN0 = 2;  // X ping buffer, MN-major box {64, 64}
 constexpr int TM_XMN1 = 3;  // X pong buffer, MN-major box {64, 64}
 constexpr int TM_GRAM = 4;  // A = X Xᵀ, K-major box {64, 128}
 constexpr int TM_POLY = 5;  // B = bA + cA², K-major box {64, 128}
-constexpr int TMAPS_PER_MAT = 6;
+// Epilogue stores: 32x32 boxes, 64-byte swizzle (one epilogue warp's chunk).
+constexpr int TM_GRAM_ST = 6;
+constexpr int TM_POLY_ST = 7;
+constexpr int TM_X0_ST = 8;
+constexpr int TM_X1_ST = 9;
+constexpr int TMAPS_PER_MAT = 10;
 
 constexpr int PREP_TILE = 64;  // prep works on 64x64 tiles of the parameter
 

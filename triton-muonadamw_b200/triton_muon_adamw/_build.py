@@ -16,6 +16,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 CSRC = HERE.parent / "csrc"
+INCLUDE = HERE.parent.parent / "include"
 OUT = HERE / "libmuonadamw_b200.so"
 SOURCES = ["capi.cu", "adamw.cu", "muon_prep.cu", "ns_gemm.cu", "muon_plan.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -33,7 +34,7 @@ def needs_rebuild() -> bool:
         return True
     t = OUT.stat().st_mtime
     deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h"))
-    deps.append(HERE.parent.parent / "include" / "muon_adamw_b200.h")
+    deps.append(INCLUDE / "muon_adamw_b200.h")
     return any(d.exists() and d.stat().st_mtime > t for d in deps)
 
 
@@ -41,7 +42,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_rebuild():
         return OUT
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+    cmd = [nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", f"-I{INCLUDE}", "-Xcompiler", "-fPIC", "-shared",
            "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
