@@ -1,0 +1,181 @@
+"""Multi-rank logic of the sharded MuonAdamW step, on CPU ranks (gloo).
+
+The partitioning (LPT owners, buckets, ZeRO-1 pieces, flat re-homing) and the
+exchange (in-place all_gather_into_tensor per flat buffer) run exactly as on
+GPUs; only the arithmetic backend is the CPU oracle, injected here.  With the
+same arithmetic, every rank must end with parameters bit-identical to a
+single-process oracle run.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle.muon_adamw_oracle import OracleMuonAdamW, adamw_update_, muon_matrix_step_
+
+ADAM_SHAPES = [(100,), (37,), (64, 3), (5,), (129,)]
+MUON_SHAPES = [(16, 24), (24, 16), (8, 8), (32, 16), (5, 7), (40, 8), (12, 12)]
+MUON = dict(lr=1e-2, beta=0.95, eps=1e-7, weight_decay=0.1, coeffs=(3.4445, -4.775, 2.0315), nesterov=True,
+            ns_steps=5, adjust_lr_fn="original")
+ADAM = dict(lr=3e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+
+
+class OracleBackend:
+    """CPU arithmetic for the sharded step (test only)."""
+
+    def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None):
+        for p, g, m, v in quads:
+            adamw_update_(p, g, m, v, lr=lr, beta1=beta1, beta2=beta2, eps=eps, weight_decay=weight_decay,
+                          bias1=bias1, bias2=bias2)
+
+    def muon(self, bucket, triples, *, adjust_lr_fn, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay,
+             timer=None):
+        for p, g, mom in triples:
+            muon_matrix_step_(p, g, mom, lr=lr, beta=beta, nesterov=nesterov, coeffs=(a, b, c), ns_steps=ns_steps,
+                              eps=eps, weight_decay=weight_decay, adjust_lr_fn=adjust_lr_fn)
+
+
+def _make(seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    adam = [torch.nn.Parameter(torch.randn(s, generator=gen) * 0.02) for s in ADAM_SHAPES]
+    muon = [torch.nn.Parameter(torch.randn(s, generator=gen) * 0.02) for s in MUON_SHAPES]
+    return adam, muon
+
+
+def _grads(step):
+    gen = torch.Generator().manual_seed(100 + step)
+    return ([torch.randn(s, generator=gen) * 1e-2 for s in ADAM_SHAPES],
+            [torch.randn(s, generator=gen) * 1e-2 for s in MUON_SHAPES])
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+# ----------------------------------------------------------------- pure logic
+def test_lpt_balances_ns_cost():
+    from oracle.muon_adamw_oracle import llama_8b_shapes
+    from triton_muon_adamw.distributed import lpt_assign, ns_cost
+    _, muon = llama_8b_shapes()
+    costs = [ns_cost(s) for s in muon]
+    for n in (2, 4, 8):
+        owner = lpt_assign(costs, n)
+        load = [sum(c for c, o in zip(costs, owner) if o == r) for r in range(n)]
+        assert max(load) / (sum(costs) / n) < 1.02, (n, load)
+        assert owner == lpt_assign(costs, n)          # deterministic on every rank
+
+
+def test_zero1_pieces_partition_every_element_once():
+    from triton_muon_adamw.distributed import ALIGN, shard_pieces, zero1_layout
+    numels = [100, 37, 192, 5, 129, 4096, 1]
+    for n in (1, 2, 3, 8):
+        offsets, shard, total = zero1_layout(numels, n)
+        assert shard % ALIGN == 0 and total == shard * n and all(o % ALIGN == 0 for o in offsets)
+        covered = [torch.zeros(k, dtype=torch.int32) for k in numels]
+        for r in range(n):
+            for i, start, length, sh in shard_pieces(offsets, numels, r * shard, (r + 1) * shard):
+                assert 0 <= sh and sh + length <= shard
+                covered[i][start:start + length] += 1
+        assert all(bool((c == 1).all()) for c in covered)
+
+
+def test_muon_layout_segments_do_not_overlap():
+    from triton_muon_adamw.distributed import ALIGN, muon_layout
+    for n, nb in ((2, 2), (3, 4), (8, 4)):
+        slots, segs = muon_layout(MUON_SHAPES, n, nb)
+        for b, seg in enumerate(segs):
+            ranges = sorted((s.offset, s.offset + s.numel) for s in slots if s.bucket == b)
+            for (a0, a1), (b0, _) in zip(ranges, ranges[1:]):
+                assert a1 <= b0
+            for s in slots:
+                if s.bucket == b:
+                    assert s.offset % ALIGN == 0
+                    assert s.owner * seg <= s.offset and s.offset + s.numel <= (s.owner + 1) * seg
+
+
+# ----------------------------------------------------------------- gloo ranks
+def _worker(rank, world, port, mode, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+        from triton_muon_adamw import AdamConfig, MuonConfig
+        from triton_muon_adamw.distributed import ShardedMuonAdamW
+        adam, muon = _make()
+        ref = OracleMuonAdamW([p.detach().clone() for p in adam], [p.detach().clone() for p in muon],
+                              adam=ADAM, muon=MUON)
+        opt = ShardedMuonAdamW(adam, muon, MuonConfig(**MUON), AdamConfig(**ADAM), dist.group.WORLD, n_buckets=2,
+                               backend=OracleBackend())
+        if mode == "die" and rank == 1:
+            raise SystemExit(0)     # leaves before the first collective
+        for step in range(2):
+            ga, gm = _grads(step)
+            for p, g in zip(adam + muon, ga + gm):
+                p.grad = g.clone()
+            opt.step()
+            ref.step(ga, gm)
+        for p, r in zip(adam + muon, ref.params_adam + ref.params_muon):
+            assert torch.equal(p.detach(), r), f"rank {rank}: parameter {tuple(p.shape)} differs"
+        sd = opt.state_dict()
+        for i, (m, v) in enumerate(zip(ref.exp_avg, ref.exp_avg_sq)):
+            assert torch.equal(sd["adam"]["state"][i]["exp_avg"], m)
+            assert torch.equal(sd["adam"]["state"][i]["exp_avg_sq"], v)
+        for i, mom in enumerate(ref.momentum):
+            assert torch.equal(sd["muon"]["state"][i]["momentum_buffer"], mom)
+        # round trip: zero the shards, load the gathered dict back, gather again
+        opt.exp_avg.zero_()
+        for t in opt.mom_segs:
+            t.zero_()
+        opt.load_state_dict(sd)
+        sd2 = opt.state_dict()
+        assert torch.equal(sd2["adam"]["state"][0]["exp_avg"], sd["adam"]["state"][0]["exp_avg"])
+        assert torch.equal(sd2["muon"]["state"][3]["momentum_buffer"], sd["muon"]["state"][3]["momentum_buffer"])
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except SystemExit:
+        q.put((rank, "left"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-800:]}"))
+
+
+def _run(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    out = {}
+    while not q.empty():
+        r, msg = q.get()
+        out[r] = msg
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_step_matches_single_process_oracle(world):
+    out = _run(world, "normal")
+    assert out == {r: "ok" for r in range(world)}, out
+
+
+def test_rank_that_leaves_surfaces_as_collective_error():
+    """A rank that exits before the exchange: the survivor's step fails with an error, it does not hang."""
+    out = _run(2, "die")
+    assert out.get(1) == "left"
+    assert out.get(0, "").split(":")[0] in ("RuntimeError", "DistBackendError", "DistError"), out

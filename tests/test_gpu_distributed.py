@@ -1,0 +1,95 @@
+"""Sharded MuonAdamW over NCCL on 2 GPUs vs the single-GPU step (needs >= 2 B200s).
+
+Every kernel is deterministic and a matrix's result does not depend on which
+rank or bucket computes it, so the sharded step must reproduce the single-GPU
+step bit for bit on every rank.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+COEFFS = (3.4445, -4.7750, 2.0315)
+ADAM_SHAPES = [(1000, 64), (64,), (300,), (64,)]
+MUON_SHAPES = [(256, 64), (64, 256), (512, 512), (128, 96), (1024, 256), (96, 96), (300, 200), (64, 64)]
+
+
+def _params(device):
+    gen = torch.Generator().manual_seed(0)
+    adam = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(device)) for s in ADAM_SHAPES]
+    muon = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(device)) for s in MUON_SHAPES]
+    return adam, muon
+
+
+def _grads(step, device):
+    gen = torch.Generator().manual_seed(50 + step)
+    return [(torch.randn(s, generator=gen) * 1e-3).to(device) for s in ADAM_SHAPES + MUON_SHAPES]
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+        mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4, betas=(0.9, 0.95))
+        adam, muon = _params(dev)
+        sharded = MuonAdamW({"adam": adam, "muon": muon}, muon_config=mc, adam_config=ac,
+                            parameter_split="explicit", process_group=dist.group.WORLD)
+        adam1, muon1 = _params(dev)
+        single = MuonAdamW({"adam": adam1, "muon": muon1}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+        for step in range(3):
+            gs = _grads(step, dev)
+            for p, p1, g in zip(adam + muon, adam1 + muon1, gs):
+                p.grad, p1.grad = g.clone(), g.clone()
+            sharded.step()
+            single.step()
+        torch.cuda.synchronize()
+        for p, p1 in zip(adam + muon, adam1 + muon1):
+            assert torch.equal(p.detach(), p1.detach()), f"rank {rank}: {tuple(p.shape)} differs"
+        assert sharded.device_status() == 0 and single.device_status() == 0
+        sd = sharded.state_dict()
+        ref = single.state_dict()
+        for i in ref["muon"]["state"]:
+            assert torch.equal(sd["muon"]["state"][i]["momentum_buffer"], ref["muon"]["state"][i]["momentum_buffer"])
+        for i in ref["adam"]["state"]:
+            assert torch.equal(sd["adam"]["state"][i]["exp_avg_sq"], ref["adam"]["state"][i]["exp_avg_sq"])
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
+def test_two_gpu_sharded_step_is_bit_identical():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    out = {}
+    while not q.empty():
+        r, msg = q.get()
+        out[r] = msg
+    assert out == {0: "ok", 1: "ok"}, out

@@ -1,0 +1,367 @@
+"""Sharded MuonAdamW step across the ranks of one node (one process per GPU).
+
+The reference is single-GPU; this module adds the partitioning a multi-GPU
+optimizer step needs, with one real exchange step:
+
+* **Muon, whole matrices.**  Every Muon matrix is updated by exactly one rank
+  (its owner).  Matrices are split into ``n_buckets`` groups in parameter
+  order, and within a bucket assigned to ranks longest-processing-time first
+  by their Newton-Schulz cost (``3m²n + m³`` per iteration), each to the least
+  loaded rank.  Only the owner keeps the momentum buffer.
+* **AdamW, ZeRO-1.**  The AdamW parameters are laid end to end in one flat
+  buffer (each tensor 64-element aligned) cut into ``world`` equal element
+  ranges; rank r updates range r and holds exp_avg/exp_avg_sq for it only.
+  A tensor may straddle two ranges; each rank updates its piece.
+* **Exchange.**  Parameters are re-homed as views into flat buffers laid out
+  so that every rank's updated elements form one contiguous segment at
+  offset ``rank * segment``: one in-place ``all_gather_into_tensor`` per
+  buffer refreshes every replica.  The AdamW gather starts right after the
+  AdamW launch and each Muon bucket's gather right after that bucket's
+  launches, so NCCL traffic over NVLink overlaps the remaining work.
+
+Gradients are expected to be identical on every rank already (data-parallel
+all-reduce upstream).  All ranks must call ``step()`` together.
+
+The arithmetic is delegated to a backend: :class:`CudaBackend` (the CUDA
+kernels) by default.  Tests of the partitioning logic on CPU ranks (gloo)
+inject a CPU checker backend instead; the optimizer itself never selects one.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from .adamw.cuda_adam import AdamWTable
+from .muon.cuda_muon import ADJUST_LR_FNS, MuonPlan, lr_scale, run_muon_plan
+
+ALIGN = 64  # elements: 256-byte alignment of every tensor inside a flat buffer
+
+
+def _round_up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+def ns_cost(shape) -> float:
+    """Newton-Schulz flops of one iteration with symmetric products: 3m²n + m³."""
+    m, n = min(shape[0], shape[1]), max(shape[0], shape[1])
+    return 3.0 * m * m * n + float(m) ** 3
+
+
+def lpt_assign(costs, n_ranks: int) -> list[int]:
+    """Longest-processing-time-first owners: largest cost to the least-loaded rank (ties: lowest rank)."""
+    load = [0.0] * n_ranks
+    owner = [0] * len(costs)
+    for i in sorted(range(len(costs)), key=lambda k: (-costs[k], k)):
+        r = min(range(n_ranks), key=lambda q: (load[q], q))
+        owner[i] = r
+        load[r] += costs[i]
+    return owner
+
+
+def split_buckets(costs, n_buckets: int) -> list[int]:
+    """Contiguous groups of (nearly) equal total cost, in parameter order."""
+    n_buckets = max(1, min(n_buckets, len(costs)))
+    total = sum(costs) or 1.0
+    bucket, acc, out = 0, 0.0, []
+    for c in costs:
+        if acc >= total * (bucket + 1) / n_buckets and bucket < n_buckets - 1:
+            bucket += 1
+        out.append(bucket)
+        acc += c
+    return out
+
+
+@dataclass
+class MuonSlot:
+    index: int    # position in the Muon parameter list
+    owner: int
+    bucket: int
+    offset: int   # element offset inside the bucket's flat buffer
+    numel: int
+
+
+def muon_layout(shapes, n_ranks: int, n_buckets: int):
+    """Owner, bucket and flat-buffer offset of every Muon matrix, and each bucket's segment size."""
+    costs = [ns_cost(s) for s in shapes]
+    buckets = split_buckets(costs, n_buckets)
+    nb = (max(buckets) + 1) if buckets else 0
+    slots = [None] * len(shapes)
+    seg_sizes = []
+    for b in range(nb):
+        idx = [i for i in range(len(shapes)) if buckets[i] == b]
+        owners = lpt_assign([costs[i] for i in idx], n_ranks)
+        fill = [0] * n_ranks
+        per_rank = [[] for _ in range(n_ranks)]
+        for i, r in zip(idx, owners):
+            per_rank[r].append(i)
+        for r in range(n_ranks):
+            for i in per_rank[r]:
+                numel = int(math.prod(shapes[i]))
+                slots[i] = MuonSlot(i, r, b, fill[r], numel)
+                fill[r] += _round_up(numel, ALIGN)
+        seg = _round_up(max(fill) if fill else 0, ALIGN)
+        seg_sizes.append(seg)
+        for i in idx:
+            slots[i].offset += slots[i].owner * seg
+    return slots, seg_sizes
+
+
+def zero1_layout(numels, n_ranks: int):
+    """Offsets of the AdamW tensors in one flat buffer and the per-rank shard size."""
+    offsets, off = [], 0
+    for n in numels:
+        offsets.append(off)
+        off += _round_up(n, ALIGN)
+    shard = _round_up(-(-off // n_ranks) if n_ranks else 0, ALIGN)
+    return offsets, shard, shard * n_ranks
+
+
+def shard_pieces(offsets, numels, lo: int, hi: int):
+    """Pieces (tensor, start in tensor, length, start in shard) of tensors intersecting [lo, hi)."""
+    out = []
+    for i, (o, n) in enumerate(zip(offsets, numels)):
+        a, b = max(o, lo), min(o + n, hi)
+        if a < b:
+            out.append((i, a - o, b - a, a - lo))
+    return out
+
+
+def _rehome(params, flat: torch.Tensor, offsets) -> None:
+    """Move each parameter's storage into ``flat`` (values copied); the Parameter objects stay the same."""
+    with torch.no_grad():
+        for p, o in zip(params, offsets):
+            view = flat[o:o + p.numel()].view_as(p)
+            view.copy_(p.data)
+            p.data = view
+
+
+# --------------------------------------------------------------------------- backends
+class CudaBackend:
+    """The product's arithmetic: the CUDA AdamW and Muon kernels."""
+
+    def __init__(self):
+        self.adam_table = AdamWTable()
+        self.plans = {}
+
+    def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None):
+        if not quads:
+            return
+        self.adam_table.ensure(quads, quads[0][0].device)
+        if timer is not None:
+            timer.mark("adamw")
+        self.adam_table.launch(lr=lr, beta1=beta1, beta2=beta2, eps=eps, weight_decay=weight_decay, bias1=bias1,
+                               bias2=bias2)
+
+    def muon(self, bucket: int, triples, *, adjust_lr_fn, beta, nesterov, a, b, c, ns_steps, eps, lr,
+             weight_decay, timer=None):
+        if not triples:
+            return
+        plan = self.plans.setdefault(bucket, MuonPlan())
+        plan.ensure(triples, adjust_lr_fn, triples[0][0].device)
+        run_muon_plan(plan, beta=beta, nesterov=nesterov, a=a, b=b, c=c, ns_steps=ns_steps, eps=eps, lr=lr,
+                      weight_decay=weight_decay, timer=timer)
+
+    def status(self) -> int:
+        st = 0
+        for plan in self.plans.values():
+            st |= plan.read_status()
+        return st
+
+
+class _Branch:
+    """Hyperparameter holder exposing the attributes of the reference's branch optimizers."""
+
+    def __init__(self, params):
+        self.model_params = list(params)
+        self._timer = None
+
+    def zero_grad(self):
+        for p in self.model_params:
+            if p.grad is not None:
+                p.grad.zero_()
+
+
+class ShardedMuonAdamW:
+    """The MuonAdamW step partitioned over a process group (see the module docstring)."""
+
+    def __init__(self, adam_params, muon_params, muon_config, adam_config, process_group, *, n_buckets=4,
+                 backend=None):
+        if muon_config.adjust_lr_fn not in ADJUST_LR_FNS:
+            raise AssertionError(f"Invalid adjust_lr_fn: {muon_config.adjust_lr_fn}")
+        for p in muon_params:
+            if p.ndim != 2:
+                raise AssertionError("Muon only supports 2D tensors")
+        for p in list(adam_params) + list(muon_params):
+            if p.dtype != torch.float32:
+                raise TypeError(f"parameters must be float32, got {p.dtype}")
+        self.pg = process_group
+        self.rank = dist.get_rank(process_group)
+        self.world = dist.get_world_size(process_group)
+        self.backend = backend if backend is not None else CudaBackend()
+        params = list(adam_params) + list(muon_params)
+        self.device = params[0].device if params else torch.device("cpu")
+
+        ad = self.adamw = _Branch(adam_params)
+        ad.lr, (ad.beta1, ad.beta2) = adam_config.lr, tuple(adam_config.betas)
+        ad.eps, ad.weight_decay, ad.step_num = adam_config.eps, adam_config.weight_decay, 0
+        mu = self.muon = _Branch(muon_params)
+        mu.lr, mu.beta, mu.eps, mu.weight_decay = muon_config.lr, muon_config.beta, muon_config.eps, muon_config.weight_decay
+        mu.a, mu.b, mu.c = muon_config.coeffs
+        mu.is_nesterov, mu.steps, mu.adjust_lr_fn = muon_config.nesterov, muon_config.ns_steps, muon_config.adjust_lr_fn
+
+        # AdamW: ZeRO-1 ranges over one flat buffer.
+        self.adam_numels = [p.numel() for p in ad.model_params]
+        self.adam_offsets, self.adam_shard, total = zero1_layout(self.adam_numels, self.world)
+        self.adam_flat = torch.zeros(total, dtype=torch.float32, device=self.device)
+        _rehome(ad.model_params, self.adam_flat, self.adam_offsets)
+        lo = self.rank * self.adam_shard
+        self.adam_pieces = shard_pieces(self.adam_offsets, self.adam_numels, lo, lo + self.adam_shard)
+        self.exp_avg = torch.zeros(self.adam_shard, dtype=torch.float32, device=self.device)
+        self.exp_avg_sq = torch.zeros(self.adam_shard, dtype=torch.float32, device=self.device)
+
+        # Muon: owner segments per bucket.
+        shapes = [tuple(p.shape) for p in mu.model_params]
+        self.slots, self.seg_sizes = muon_layout(shapes, self.world, n_buckets)
+        self.muon_flats = [torch.zeros(self.world * seg, dtype=torch.float32, device=self.device)
+                           for seg in self.seg_sizes]
+        with torch.no_grad():
+            for p, s in zip(mu.model_params, self.slots):
+                view = self.muon_flats[s.bucket][s.offset:s.offset + s.numel].view_as(p)
+                view.copy_(p.data)
+                p.data = view
+        # Momentum for owned matrices, laid out like the owner's parameter segment.
+        self.mom_segs = [torch.zeros(seg, dtype=torch.float32, device=self.device) for seg in self.seg_sizes]
+        mu.momentum = {}
+        for p, s in zip(mu.model_params, self.slots):
+            if s.owner == self.rank:
+                o = s.offset - self.rank * self.seg_sizes[s.bucket]
+                mu.momentum[p] = self.mom_segs[s.bucket][o:o + s.numel].view_as(p)
+
+    # ------------------------------------------------------------------ step
+    def _adam_quads(self):
+        quads = []
+        ad = self.adamw
+        for i, start, length, sh in self.adam_pieces:
+            p = ad.model_params[i]
+            if p.grad is None:
+                continue
+            o = self.adam_offsets[i] + start
+            quads.append((self.adam_flat[o:o + length], p.grad.reshape(-1)[start:start + length],
+                          self.exp_avg[sh:sh + length], self.exp_avg_sq[sh:sh + length]))
+        return quads
+
+    def _bucket_triples(self, b):
+        mu = self.muon
+        out = []
+        for p, s in zip(mu.model_params, self.slots):
+            if s.bucket == b and s.owner == self.rank and p.grad is not None and p.numel() > 0:
+                out.append((p.data, p.grad, mu.momentum[p]))
+        return out
+
+    def _gather(self, flat: torch.Tensor, seg: int):
+        mine = flat[self.rank * seg:(self.rank + 1) * seg]
+        return dist.all_gather_into_tensor(flat, mine, group=self.pg, async_op=True)
+
+    @torch.no_grad()
+    def step(self):
+        ad, mu = self.adamw, self.muon
+        ad.step_num += 1
+        works = []
+        bias1, bias2 = 1 - ad.beta1 ** ad.step_num, 1 - ad.beta2 ** ad.step_num
+        if self.adam_shard:
+            self.backend.adamw(self._adam_quads(), lr=ad.lr, beta1=ad.beta1, beta2=ad.beta2, eps=ad.eps,
+                               weight_decay=ad.weight_decay, bias1=bias1, bias2=bias2, timer=ad._timer)
+            works.append(self._gather(self.adam_flat, self.adam_shard))
+        for b, seg in enumerate(self.seg_sizes):
+            self.backend.muon(b, self._bucket_triples(b), adjust_lr_fn=mu.adjust_lr_fn, beta=mu.beta,
+                              nesterov=mu.is_nesterov, a=mu.a, b=mu.b, c=mu.c, ns_steps=mu.steps, eps=mu.eps,
+                              lr=mu.lr, weight_decay=mu.weight_decay, timer=mu._timer)
+            if seg:
+                works.append(self._gather(self.muon_flats[b], seg))
+        for w in works:
+            w.wait()
+
+    # ------------------------------------------------------------------ introspection
+    def owned_muon_shapes(self):
+        return [tuple(p.shape) for p, s in zip(self.muon.model_params, self.slots)
+                if s.owner == self.rank and p.grad is not None]
+
+    def adam_shard_numel(self):
+        return sum(length for _, _, length, _ in self.adam_pieces)
+
+    def local_grad_tensors(self):
+        """Gradient pieces this rank reads in a step (what a host-resident pipeline must copy in)."""
+        out = [p.grad.reshape(-1)[start:start + length]
+               for i, start, length, _ in self.adam_pieces
+               for p in [self.adamw.model_params[i]] if p.grad is not None]
+        out += [g for _, g, _ in (t for b in range(len(self.seg_sizes)) for t in self._bucket_triples(b))]
+        return out
+
+    def status(self) -> int:
+        return self.backend.status() if hasattr(self.backend, "status") else 0
+
+    # ------------------------------------------------------------------ checkpoint
+    @torch.no_grad()
+    def state_dict(self):
+        """Full (gathered) state in the layout of PyTorchMuonAdamW.state_dict(); collective."""
+        from .checkpoint import _adam_group, _muon_group  # noqa: PLC0415
+        ad, mu = self.adamw, self.muon
+        full_m = torch.empty(self.adam_shard * self.world, dtype=torch.float32, device=self.device)
+        full_v = torch.empty_like(full_m)
+        dist.all_gather_into_tensor(full_m, self.exp_avg, group=self.pg)
+        dist.all_gather_into_tensor(full_v, self.exp_avg_sq, group=self.pg)
+        adam_state = {}
+        if ad.step_num > 0:
+            for i, p in enumerate(ad.model_params):
+                o, n = self.adam_offsets[i], self.adam_numels[i]
+                adam_state[i] = {"step": torch.tensor(float(ad.step_num), dtype=torch.float32, device=p.device),
+                                 "exp_avg": full_m[o:o + n].view_as(p).clone(),
+                                 "exp_avg_sq": full_v[o:o + n].view_as(p).clone()}
+        fulls = []
+        for seg, mom in zip(self.seg_sizes, self.mom_segs):
+            f = torch.empty(seg * self.world, dtype=torch.float32, device=self.device)
+            dist.all_gather_into_tensor(f, mom, group=self.pg)
+            fulls.append(f)
+        muon_state = {i: {"momentum_buffer": fulls[s.bucket][s.offset:s.offset + s.numel].view_as(p).clone()}
+                      for i, (p, s) in enumerate(zip(mu.model_params, self.slots))}
+        return {"adam": {"state": adam_state, "param_groups": [_adam_group(ad, len(ad.model_params))]},
+                "muon": {"state": muon_state, "param_groups": [_muon_group(mu, len(mu.model_params))]}}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd):
+        """Load a full state dict (every rank passes the same one); each rank keeps its shard."""
+        ad, mu = self.adamw, self.muon
+        if "adam" in sd:
+            a = sd["adam"]
+            g = a["param_groups"][0]
+            ad.lr, (ad.beta1, ad.beta2), ad.eps, ad.weight_decay = g["lr"], tuple(g["betas"]), g["eps"], g["weight_decay"]
+            steps = []
+            for i, start, length, sh in self.adam_pieces:
+                st = a["state"].get(i)
+                if st is None:
+                    continue
+                self.exp_avg[sh:sh + length].copy_(st["exp_avg"].reshape(-1)[start:start + length])
+                self.exp_avg_sq[sh:sh + length].copy_(st["exp_avg_sq"].reshape(-1)[start:start + length])
+            for st in a["state"].values():
+                steps.append(int(float(st["step"])))
+            ad.step_num = max(steps) if steps else 0
+        if "muon" in sd:
+            m = sd["muon"]
+            g = m["param_groups"][0]
+            mu.lr, mu.weight_decay, mu.beta, mu.is_nesterov = g["lr"], g["weight_decay"], g["momentum"], g["nesterov"]
+            if "ns_coefficients" in g:
+                mu.a, mu.b, mu.c = g["ns_coefficients"]
+            mu.eps, mu.steps = g.get("eps", mu.eps), g.get("ns_steps", mu.steps)
+            mu.adjust_lr_fn = g.get("adjust_lr_fn") or "original"
+            for i, p in enumerate(mu.model_params):
+                st = m["state"].get(i)
+                if st is not None and p in mu.momentum:
+                    mu.momentum[p].copy_(st["momentum_buffer"])
+
+
+__all__ = ["ShardedMuonAdamW", "CudaBackend", "lpt_assign", "split_buckets", "muon_layout", "zero1_layout",
+           "shard_pieces", "ns_cost", "lr_scale"]

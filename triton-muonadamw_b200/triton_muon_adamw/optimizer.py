@@ -187,6 +187,8 @@ class MuonAdamW(TritonMuon, TritonAdamW):
 
     def device_status(self, clear: bool = True) -> int:
         """Error bits recorded by the Muon kernels since the last read (0 = healthy)."""
+        if self.distributed is not None:
+            return self.distributed.status()
         return self.muon.device_status(clear)
 
     # -- checkpointing -----------------------------------------------------
