@@ -296,47 +296,52 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
-    # Per-kernel timing: one more timed pass with events between every launch.
+    # Per-kernel timing: one more pass with CUDA events between every launch.
     timer = PhaseTimer()
     opt_branch_timer(opt, timer)
+    timing_steps = max(1, min(args.steps, 3))
     barrier()
-    for _ in range(max(1, min(args.steps, 3))):
+    for _ in range(timing_steps):
         opt.step()
     barrier()
     opt_branch_timer(opt, None)
     per = timer.durations()
 
-    # Work accounting (this rank's share).
+    # Work accounting (this rank's share), per step.
     owned = owned_shapes(opt)
     flops = {"gram": 0.0, "poly": 0.0, "update": 0.0}
     elems_muon = 0
     for s in owned:
         f = ns_flops_sym(s)
         for k in flops:
-            flops[k] += f[k]
+            flops[k] += f[k] * args.ns_steps
         elems_muon += math.prod(s)
     adam_elems = adam_elems_local(opt)
     hbm, tf_burst, tf_sus, peak_src = measured_peaks()
     kernels = {}
+
+    def phase(label):
+        d = per.get(label, [])
+        return (sum(d) / timing_steps, len(d) / timing_steps) if d else (0.0, 0.0)
+
     for k in ("gram", "poly", "update"):
-        d = per.get(k, [])
-        if d:
-            avg = sum(d) / len(d)
-            kernels[f"ns_gemm_{k}"] = {"launches": len(d), "avg_ms": round(avg, 4),
-                                       "tflops": round(flops[k] / (avg * 1e-3) / 1e12, 1),
-                                       "frac_sustained": round(flops[k] / (avg * 1e-3) / 1e12 / tf_sus, 3)}
-    if per.get("adamw"):
-        avg = sum(per["adamw"]) / len(per["adamw"])
-        gbs = 28.0 * adam_elems / (avg * 1e-3) / 1e9
-        kernels["adamw_multi"] = {"launches": len(per["adamw"]), "avg_ms": round(avg, 4), "gbs": round(gbs, 1),
+        ms_k, n_k = phase(k)
+        if n_k:
+            tfl = flops[k] / (ms_k * 1e-3) / 1e12
+            kernels[f"ns_gemm_{k}"] = {"launches_per_step": n_k, "ms_per_step": round(ms_k, 3),
+                                       "avg_launch_ms": round(ms_k / n_k, 4), "tflops": round(tfl, 1),
+                                       "frac_sustained": round(tfl / tf_sus, 3)}
+    ms_a, n_a = phase("adamw")
+    if n_a:
+        gbs = 28.0 * adam_elems / (ms_a * 1e-3) / 1e9
+        kernels["adamw_multi"] = {"launches_per_step": n_a, "ms_per_step": round(ms_a, 3), "gbs": round(gbs, 1),
                                   "frac": round(gbs / hbm, 3), "bytes_per_elem": 28}
-    if per.get("prep"):
-        avg = sum(per["prep"]) / len(per["prep"])
-        gbs = 14.0 * elems_muon / (avg * 1e-3) / 1e9
-        kernels["muon_prep"] = {"launches": len(per["prep"]), "avg_ms": round(avg, 4), "gbs": round(gbs, 1),
+    ms_p, n_p = phase("prep")
+    if n_p:
+        gbs = 14.0 * elems_muon / (ms_p * 1e-3) / 1e9
+        kernels["muon_prep"] = {"launches_per_step": n_p, "ms_per_step": round(ms_p, 3), "gbs": round(gbs, 1),
                                 "frac": round(gbs / hbm, 3), "bytes_per_elem": 14}
-    # per Newton-Schulz iteration (one gram + one poly + one update launch over all matrices)
-    ns_ms = sum(sum(per.get(k, [])) for k in ("gram", "poly", "update")) / max(1, len(per.get("update", [1])))
+    ns_ms = sum(phase(k)[0] for k in ("gram", "poly", "update"))
     ns_total = sum(flops.values())
     upd = kernels.get("ns_gemm_update", {})
     traffic = ncu_traffic("ns_gemm_update", args.config)
@@ -345,12 +350,11 @@ def main():
                 "frac": upd.get("frac_sustained"), "peak_kind": f"{peak_src} sustained bf16",
                 "traffic": traffic, "ns_all_tflops": round(ns_total / (ns_ms * 1e-3) / 1e12, 1) if ns_ms else None,
                 "ns_all_frac_sustained": round(ns_total / (ns_ms * 1e-3) / 1e12 / tf_sus, 3) if ns_ms else None,
-                "ns_ms_per_step": round(ns_ms * args.ns_steps, 3),
-                "ns_flops_per_step": ns_total * args.ns_steps}
+                "ns_ms_per_step": round(ns_ms, 3), "ns_flops_per_step": ns_total}
+    launches_per_step = sum(len(v) for v in per.values()) / timing_steps
 
     # End to end: this step's gradients from pinned host memory, result read back.
     e2e = run_e2e(opt, model, dev, args, barrier, world)
-    launches_per_step = (1 if n_adam else 0) + ((2 + 3 * args.ns_steps) if owned else 0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -369,7 +373,7 @@ def main():
                        "parallelism": "single-gpu" if world == 1 else f"muon-owner+zero1-adamw x{world}",
                        "l2": "inputs (fp32 grads/params/momentum, > 100 GB) exceed L2; no flush needed",
                        "elementwise_dtype": "fp32"},
-            "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clock_info, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
