@@ -344,11 +344,11 @@ def main():
     ns_ms = sum(phase(k)[0] for k in ("gram", "poly", "update"))
     ns_total = sum(flops.values())
     upd = kernels.get("ns_gemm_update", {})
-    traffic = ncu_traffic("ns_gemm_update", args.config)
+    traffic, traffic_how = ncu_traffic("ns_gemm_update", args.config)
     roofline = {"kernel": "ns_gemm_kernel<UPDATE> (tcgen05 B·X + a·X epilogue)", "bound": "tensor",
                 "achieved": upd.get("tflops"), "peak": tf_sus, "unit": "TFLOP/s",
                 "frac": upd.get("frac_sustained"), "peak_kind": f"{peak_src} sustained bf16",
-                "traffic": traffic, "ns_all_tflops": round(ns_total / (ns_ms * 1e-3) / 1e12, 1) if ns_ms else None,
+                "traffic": traffic, "traffic_source": traffic_how, "ns_all_tflops": round(ns_total / (ns_ms * 1e-3) / 1e12, 1) if ns_ms else None,
                 "ns_all_frac_sustained": round(ns_total / (ns_ms * 1e-3) / 1e12 / tf_sus, 3) if ns_ms else None,
                 "ns_ms_per_step": round(ns_ms, 3), "ns_flops_per_step": ns_total}
     launches_per_step = sum(len(v) for v in per.values()) / timing_steps
@@ -401,14 +401,15 @@ def adam_elems_local(opt):
 
 
 def ncu_traffic(kernel, config):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (None if not captured)."""
     p = ROOT / "profiles" / "ncu_traffic.json"
     if not p.exists():
-        return None
+        return None, None
     try:
-        d = json.loads(p.read_text())
-        return d.get(config, {}).get(kernel)
+        d = json.loads(p.read_text()).get(config, {}).get(kernel)
     except (ValueError, OSError):
-        return None
+        return None, None
+    return (d["bytes_per_launch"], d["how"]) if d else (None, None)
 
 
 def run_e2e(opt, model, dev, args, barrier, world):
