@@ -64,15 +64,15 @@ def test_plan_sizes_for_the_8b_shapes():
     info = _lib.MuonPlanInfo()
     _lib.check(lib.mad_muon_plan_size(arr, len(muon), ctypes.byref(info)))
 
-    def tri(m):
-        tms, tns = -(-m // 128), -(-m // 256)
-        return sum(min(tms, 2 * tn + 2) for tn in range(tns))
+    def tri(m):           # 256 x 256 pair tiles on or above the diagonal
+        t = -(-m // 256)
+        return t * (t + 1) // 2
 
     counts = {}
     for s in muon:
         counts[s] = counts.get(s, 0) + 1
     exp_gram = sum(cnt * tri(min(s)) for s, cnt in counts.items())
-    exp_upd = sum(cnt * (-(-min(s) // 128)) * (-(-max(s) // 256)) for s, cnt in counts.items())
+    exp_upd = sum(cnt * (-(-min(s) // 256)) * (-(-max(s) // 256)) for s, cnt in counts.items())
     assert info.gram_tiles == exp_gram == info.poly_tiles
     assert info.update_tiles == exp_upd
     # bf16 workspaces: 2 iterates (m x n) + A, B (m x m), rows padded to 64

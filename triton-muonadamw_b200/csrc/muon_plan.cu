@@ -29,7 +29,8 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
 
 namespace {
 
-constexpr int GEMM_BM = 128, GEMM_BN = 256;
+// Output tiles are computed by CTA pairs: 256 x 256 (each CTA 128 rows).
+constexpr int GEMM_BM = 256, GEMM_BN = 256;
 
 inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -56,11 +57,9 @@ int64_t work_bytes_of(const Shape& s) {
 }
 
 int64_t gram_tiles_of(const Shape& s) {
-  // Tiles (tm, tn) of the m x m output touching the upper triangle in 128-blocks: 2*tn + 1 >= tm.
-  const int64_t tms = (s.m + GEMM_BM - 1) / GEMM_BM, tns = (s.m + GEMM_BN - 1) / GEMM_BN;
-  int64_t cnt = 0;
-  for (int64_t tn = 0; tn < tns; ++tn) cnt += std::min<int64_t>(tms, 2 * tn + 2);
-  return cnt;
+  // 256 x 256 tiles (tm, tn) of the m x m output on or above the diagonal: tn >= tm.
+  const int64_t t = (s.m + GEMM_BM - 1) / GEMM_BM;
+  return t * (t + 1) / 2;
 }
 
 int64_t update_tiles_of(const Shape& s) {
@@ -257,7 +256,7 @@ extern "C" int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* 
       const int64_t tms = (s.m + GEMM_BM - 1) / GEMM_BM;
       const int64_t tns = ((triangle ? s.m : s.n) + GEMM_BN - 1) / GEMM_BN;
       for (int64_t tn = 0; tn < tns; ++tn) {
-        const int64_t tm_end = triangle ? std::min<int64_t>(tms, 2 * tn + 2) : tms;
+        const int64_t tm_end = triangle ? std::min<int64_t>(tms, tn + 1) : tms;
         for (int64_t tmi = 0; tmi < tm_end; ++tmi) {
           out[k].mat = i;
           out[k].tm = static_cast<int32_t>(tmi);

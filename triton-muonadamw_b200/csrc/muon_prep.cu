@@ -57,36 +57,49 @@ __global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __rest
 
     float ss = 0.f;
     const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
+    float xv[4][4];
+    if (full) {
+      // All loads of the tile first (8 x 16 B in flight per thread), then compute and store.
+      float4 gv[4], mv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+        gv[i] = __ldcs(reinterpret_cast<const float4*>(g + off));
+        mv[i] = __ldcs(reinterpret_cast<const float4*>(mom + off));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+        xv[i][0] = prep_update(gv[i].x, mv[i].x, s);
+        xv[i][1] = prep_update(gv[i].y, mv[i].y, s);
+        xv[i][2] = prep_update(gv[i].z, mv[i].z, s);
+        xv[i][3] = prep_update(gv[i].w, mv[i].w, s);
+        __stcs(reinterpret_cast<float4*>(mom + off), mv[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = r0 + i * 16 + (t >> 4), c = c0 + cl;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          xv[i][k] = 0.f;
+          if (r < rows && c + k < cols) {
+            const int64_t off = static_cast<int64_t>(r) * cols + c + k;
+            float mvv = mom[off];
+            xv[i][k] = prep_update(g[off], mvv, s);
+            mom[off] = mvv;
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int rl = i * 16 + (t >> 4);
       const int r = r0 + rl, c = c0 + cl;
-      float xv[4];
-      if (full) {
-        const int64_t off = static_cast<int64_t>(r) * cols + c;
-        const float4 gv = __ldcs(reinterpret_cast<const float4*>(g + off));
-        float4 mv = *reinterpret_cast<const float4*>(mom + off);
-        xv[0] = prep_update(gv.x, mv.x, s);
-        xv[1] = prep_update(gv.y, mv.y, s);
-        xv[2] = prep_update(gv.z, mv.z, s);
-        xv[3] = prep_update(gv.w, mv.w, s);
-        *reinterpret_cast<float4*>(mom + off) = mv;
-      } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          xv[k] = 0.f;
-          if (r < rows && c + k < cols) {
-            const int64_t off = static_cast<int64_t>(r) * cols + c + k;
-            float mv = mom[off];
-            xv[k] = prep_update(g[off], mv, s);
-            mom[off] = mv;
-          }
-        }
-      }
       __nv_bfloat16 xb[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        xb[k] = __float2bfloat16_rn(xv[k]);
+        xb[k] = __float2bfloat16_rn(xv[i][k]);
         const float q = __bfloat162float(xb[k]);
         ss = fmaf(q, q, ss);
       }

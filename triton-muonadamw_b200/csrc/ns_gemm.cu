@@ -15,12 +15,18 @@
 // of X' (triton_muon.py:365-372): p -= (lr·wd)·p ; p -= scaled_lr·bf16(X'),
 // transposed back for tall matrices.
 //
-// CTA tile 128 x 256, K step 64 (one 128-byte swizzle atom of bf16), 4-stage
-// TMA ring (48 KB/stage), accumulators double-buffered in TMEM (2 x 256 of
-// the 512 columns) so the epilogue of tile i overlaps the MMAs of tile i+1.
-// Warp 0 issues TMA, warp 1 issues tcgen05.mma (one thread), warps 2-9 drain
-// TMEM (one accumulator row and half the columns per thread).  Operands: X Xᵀ and A A read two
-// K-major tiles; B X reads B K-major and X MN-major (its rows are the K index).
+// CTA pairs (clusters of 2) compute 256 x 256 tiles with tcgen05.mma.cta_group::2:
+// each CTA loads its own 128 rows of the A operand and half (128 columns) of
+// the B operand per K step of 64, so an SM moves 32 KB per step instead of
+// the 48 KB a single-CTA 128 x 256 tile needs -- a third less operand traffic
+// per flop, with no multicast load anywhere.  6-stage TMA ring per CTA;
+// accumulators (each CTA: its 128 rows x 256 columns) double-buffered in TMEM
+// so the epilogue of tile i overlaps the MMAs of tile i+1.  Warp 0 issues TMA
+// (both CTAs; completion counted on the leader's barrier), warp 1 of the
+// leader issues the pair MMAs (one thread), warps 2-9 of both CTAs drain TMEM
+// (one accumulator row and half the columns per thread).  Operands: X Xᵀ and
+// A A read two K-major tiles; B X reads B K-major and X MN-major (its rows are
+// the K index).
 #include <cuda_runtime.h>
 
 #include "capi_common.h"
@@ -30,10 +36,12 @@
 namespace mad {
 namespace ns {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
+constexpr int PAIR_M = 2 * BM;          // rows of a pair tile
+constexpr int A_BYTES = BM * BK * 2;    // 16 KB: this CTA's 128 rows of A
+constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB: this CTA's 128 columns of B
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t PAIR_TX_BYTES = 2 * STAGE_BYTES;  // both CTAs' fills, counted on the leader's barrier
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int EPI_WARPS = 8;
 constexpr int EPI_THREADS = EPI_WARPS * 32;
@@ -73,12 +81,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 template <int MODE>
 __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                              volatile int* abort_flag) {
-  int stage = 0, issued = 0;
+                                              uint32_t rank, volatile int* abort_flag) {
+  int stage = 0;
   uint32_t phase = 0;
   const int cur = args.iter & 1;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
   bool ok = true;
-  for (int t = blockIdx.x; t < args.n_tiles && ok; t += gridDim.x) {
+  for (int t = cid; t < args.n_tiles && ok; t += ncl) {
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
     const CUtensorMap* maps = args.tmaps + md.tmap_base;
@@ -94,6 +103,8 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
     }
     tma_acquire_desc(tmA);
     if (tmB != tmA) tma_acquire_desc(tmB);
+    const int arow = tr.tm * PAIR_M + static_cast<int>(rank) * BM;     // this CTA's A rows
+    const int bcol = tr.tn * BN + static_cast<int>(rank) * (BN / 2);   // this CTA's B columns
     const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_PRODUCER) || *abort_flag) {
@@ -103,37 +114,36 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
       }
       uint8_t* sa = ring + stage * STAGE_BYTES;
       uint8_t* sb = sa + A_BYTES;
-      mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-      tma_load_2d(sa, tmA, &full[stage], kb * BK, tr.tm * BM);
+      // Both CTAs' fills complete on the leader's barrier; the leader arms it for both.
+      const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+      if (rank == 0) mbar_arrive_expect_tx(&full[stage], PAIR_TX_BYTES);
+      tma_load_2d_pair(sa, tmA, bar, kb * BK, arow);
       if (is_update<MODE>()) {
-#pragma unroll
-        for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * (64 * BK * 2), tmB, &full[stage], tr.tn * BN + j * 64, kb * BK);
+        tma_load_2d_pair(sb, tmB, bar, bcol, kb * BK);
+        tma_load_2d_pair(sb + 64 * BK * 2, tmB, bar, bcol + 64, kb * BK);
       } else {
-        tma_load_2d(sb, tmB, &full[stage], kb * BK, tr.tn * BN);
-        tma_load_2d(sb + BM * BK * 2, tmB, &full[stage], kb * BK, tr.tn * BN + BM);
+        tma_load_2d_pair(sb, tmB, bar, kb * BK, bcol);
       }
-      ++issued;
       if (++stage == STAGES) {
         stage = 0;
         phase ^= 1u;
       }
     }
   }
-  // Make sure no copy into this CTA's shared memory is still in flight when it
-  // exits (only possible after an abort): wait for the last fills to land.
-  for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-    mbar_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1), args.status, DEV_ERR_MBAR_TIMEOUT_DRAIN);
 }
 
+// Leader CTA only: one thread issues the pair MMAs and returns each smem stage
+// and each finished accumulator to both CTAs (two commits, one per CTA).
 template <int MODE>
 __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                          uint64_t* tfull, uint64_t* tempty, uint64_t* drain, uint32_t tmem_base,
                                          volatile int* abort_flag) {
-  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, is_update<MODE>());
+  constexpr uint32_t IDESC = idesc_bf16_f32(PAIR_M, BN, false, is_update<MODE>());
   int stage = 0, lt = 0;
   uint32_t phase = 0;
   bool ok = true;
-  for (int t = blockIdx.x; t < args.n_tiles && ok; t += gridDim.x, ++lt) {
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  for (int t = cid; t < args.n_tiles && ok; t += ncl, ++lt) {
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
     const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
@@ -158,19 +168,25 @@ __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, ui
       for (int kk = 0; kk < BK / 16; ++kk) {
         const uint64_t ad = smem_desc_sw128(sa + kk * 32, 16, 1024);
         const uint64_t bd = is_update<MODE>() ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
-                                             : smem_desc_sw128(sb + kk * 32, 16, 1024);
-        tc_mma_bf16(d_tmem, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                                              : smem_desc_sw128(sb + kk * 32, 16, 1024);
+        tc_mma_bf16_pair(d_tmem, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
       }
-      tc_commit(&empty[stage]);
+      const uint32_t e = smem_u32(&empty[stage]);
+      tc_commit_pair(mapa_shared(e, 0));
+      tc_commit_pair(mapa_shared(e, 1));
       if (++stage == STAGES) {
         stage = 0;
         phase ^= 1u;
       }
     }
-    if (ok) tc_commit(&tfull[acc]);
+    if (ok) {
+      const uint32_t f = smem_u32(&tfull[acc]);
+      tc_commit_pair(mapa_shared(f, 0));
+      tc_commit_pair(mapa_shared(f, 1));
+    }
   }
   // Every MMA this thread issued must finish before TMEM is released.
-  tc_commit(drain);
+  tc_commit_pair(mapa_shared(smem_u32(drain), 0));
   mbar_wait(drain, 0u, args.status, DEV_ERR_MBAR_TIMEOUT_DRAIN);
 }
 
@@ -334,18 +350,21 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
 // while the previous chunk is finished.
 template <int MODE>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull, uint64_t* tempty,
-                                              uint32_t tmem_base, uint8_t* stage, volatile int* abort_flag) {
+                                              uint32_t tmem_base, uint8_t* stage, uint32_t rank,
+                                              volatile int* abort_flag) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int half = (warp - 2) >> 2;
-  const int row_in_tile = quad * 32 + lane;
+  const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
   int lt = 0;
-  for (int t = blockIdx.x; t < args.n_tiles; t += gridDim.x, ++lt) {
+  for (int t = cid; t < args.n_tiles; t += ncl, ++lt) {
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
     const int acc_buf = lt & 1;
     const uint32_t acc_phase = static_cast<uint32_t>((lt >> 1) & 1);
-    const int grow0 = tr.tm * BM + quad * 32;
+    const int rowblk = (tr.tm * PAIR_M + static_cast<int>(rank) * BM) / BM;  // this CTA's 128-row block
+    const int grow0 = rowblk * BM + quad * 32;
     const int grow = grow0 + lane;
     const bool row_ok = grow < md.m;
     const int col0 = tr.tn * BN + half * 128;
@@ -354,8 +373,8 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     const int blk = col0 / BM;
     int nch = (col0 < limit) ? (limit - col0 + 31) / 32 : 0;
     if (nch > 4) nch = 4;
-    if (!is_update<MODE>() && blk < tr.tm) nch = 0;
-    const bool mirror = !is_update<MODE>() && blk > tr.tm;
+    if (!is_update<MODE>() && blk < rowblk) nch = 0;
+    const bool mirror = !is_update<MODE>() && blk > rowblk;
     // The parameter-writing update keeps one chunk of global inputs in flight, the others two.
     constexpr bool PREFETCH_NEXT = MODE != UPDATE_LAST;
 
@@ -388,15 +407,20 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
         chunk_finish<MODE>(args, md, grow0, grow, row_ok, col0 + 32 * c, mirror, acc[c & 1], in[c & 1], stage);
       if (c + 1 < nch) tmem_ld_wait(acc[(c + 1) & 1]);
     }
+    // Accumulator drained: one arrival per warp on the leader's barrier.
     tc_fence_before();
-    mbar_arrive(&tempty[acc_buf]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(tempty_leader[acc_buf]);
   }
   if (lane == 0) bulk_wait_all();  // every output store has landed before the CTA retires
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_constant__ GemmArgs args) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    ns_gemm_kernel(const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
+  // Same layout in both CTAs of the pair: the pair MMA and the leader-side
+  // barriers are addressed by identical shared-memory offsets.
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_out = ring + STAGES * STAGE_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + EPI_WARPS * STAGE_OUT_BYTES);
@@ -408,6 +432,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -415,33 +440,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], EPI_THREADS);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) producer_loop<MODE>(args, ring, full, empty, abort_flag);
+    if (lane == 0) producer_loop<MODE>(args, ring, full, empty, rank, abort_flag);
   } else if (warp == 1) {
-    if (lane == 0) mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, abort_flag);
+    if (lane == 0 && rank == 0) mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, abort_flag);
   } else {
-    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * STAGE_OUT_BYTES, abort_flag);
+    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * STAGE_OUT_BYTES, rank, abort_flag);
+  }
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    // After an abort a peer may still have copies in flight into this CTA's
+    // shared memory: give them time to land (bounded) before retiring.
+    const long long t0 = clock64();
+    while (clock64() - t0 < 400000) {
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // neither CTA retires while the pair still uses its memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -451,8 +484,29 @@ static int launch(const GemmArgs& args, cudaStream_t stream, const char* name) {
   if (cudaFuncSetAttribute(ns_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return fail_cuda("cudaFuncSetAttribute(ns_gemm_kernel)");
-  const int grid = args.n_tiles < num_sms() ? args.n_tiles : num_sms();
-  ns_gemm_kernel<MODE><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(args);
+  // One CTA pair per two SMs: as many pairs as can be co-resident, capped by the tile count.
+  static int max_pairs[16] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int pairs = (dev < 16) ? max_pairs[dev] : 0;
+  if (pairs == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&pairs, ns_gemm_kernel<MODE>, &cfg) != cudaSuccess || pairs <= 0)
+      return fail_cuda("cudaOccupancyMaxActiveClusters(ns_gemm_kernel)");
+    if (dev < 16) max_pairs[dev] = pairs;
+  }
+  const int grid_pairs = args.n_tiles < pairs ? args.n_tiles : pairs;
+  ns_gemm_kernel<MODE><<<2 * grid_pairs, NUM_THREADS, SMEM_BYTES, stream>>>(args);
   return check_launch(name);
 }
 
