@@ -153,6 +153,21 @@ int mad_ns_update(const mad_muon_plan_info* info, void* dev_table, int32_t iter,
 int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float a,
                         float b, float c, int32_t ns_steps, float eps, double lr, double weight_decay, void* stream);
 
+/* The Muon step of ONE matrix without any allocation (no counterpart in the
+ * reference).  For callers that cannot allocate at step time -- code under a
+ * custom or pre-sized allocator, or a foreign-language host with no allocator
+ * binding: the plan and the bf16 workspaces live in a static device array of
+ * about 9.3 MB that every GPU loading this library keeps until exit.
+ * Limit: rows*cols <= 1,048,576 and min(rows, cols) <= 1024 (MAD_ERR_INVALID
+ * otherwise).  Same arguments and results as planning the one matrix with
+ * mad_muon_plan and calling mad_muon_step_multi; lr_scale as in
+ * mad_muon_matrix.  The first call on a device resolves the array's address
+ * for that device, so make it before any stream capture.  Each call uploads
+ * its plan synchronously; calls that overlap on the GPU race on the array. */
+int mad_muon_step_noalloc(float* param, const float* grad, float* momentum, int64_t rows, int64_t cols,
+                          double lr_scale, double beta, int32_t nesterov, float a, float b, float c, int32_t ns_steps,
+                          float eps, double lr, double weight_decay, void* stream);
+
 /* Copies the plan's device status word to *status (synchronises `stream`)
  * and, if clear != 0, resets it.  Non-zero bits mean a kernel gave up
  * waiting on a barrier; the step's results are then invalid. */

@@ -66,6 +66,9 @@ SIGNATURES = {
     "mad_muon_step_multi": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32, c_float,
                                            c_float, c_float, c_int32, c_float, ctypes.c_double, ctypes.c_double,
                                            c_void_p]),
+    "mad_muon_step_noalloc": (ctypes.c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, ctypes.c_double,
+                                             ctypes.c_double, c_int32, c_float, c_float, c_float, c_int32, c_float,
+                                             ctypes.c_double, ctypes.c_double, c_void_p]),
     "mad_muon_read_status": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.POINTER(ctypes.c_uint32),
                                             c_int32, c_void_p]),
 }
