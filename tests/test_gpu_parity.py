@@ -296,3 +296,27 @@ def test_llama8b_shapes_vs_torch_bf16(cuda_device, shape):
     err = float((o_gpu - o_ref).norm() / o_ref.norm())
     assert err < 2e-2, f"rel Frobenius error {err:.3e}"
     assert opt.device_status() == 0
+
+
+def test_step_from_host_matches_step(cuda_device):
+    """Host-resident gradients (pipelined copies) give exactly the result of step() on device gradients."""
+    from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+    gen = torch.Generator().manual_seed(21)
+    adam_shapes, muon_shapes = [(300, 64), (64,)], [(256, 64), (64, 256), (512, 512), (96, 200), (1024, 256)]
+    init = [torch.randn(s, generator=gen) * 0.02 for s in adam_shapes + muon_shapes]
+    mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4)
+    a = [torch.nn.Parameter(t.clone().to(cuda_device)) for t in init]
+    b = [torch.nn.Parameter(t.clone().to(cuda_device)) for t in init]
+    na = len(adam_shapes)
+    oa = MuonAdamW({"adam": a[:na], "muon": a[na:]}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+    ob = MuonAdamW({"adam": b[:na], "muon": b[na:]}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+    for step in range(2):
+        grads = [torch.randn(t.shape, generator=gen) * 1e-3 for t in init]
+        for p, g in zip(a, grads):
+            p.grad = g.to(cuda_device)
+        oa.step()
+        ob.step_from_host({p: g.pin_memory() for p, g in zip(b, grads)})
+        torch.cuda.synchronize()
+        for p, q in zip(a, b):
+            assert torch.equal(p.detach(), q.detach())
+    assert oa.device_status() == 0 and ob.device_status() == 0

@@ -63,15 +63,25 @@ def lpt_assign(costs, n_ranks: int) -> list[int]:
 
 
 def split_buckets(costs, n_buckets: int) -> list[int]:
-    """Contiguous groups of (nearly) equal total cost, in parameter order."""
+    """Contiguous groups in parameter order with decreasing total cost (weights n, n-1, ..., 1).
+
+    Each bucket's all-gather overlaps the compute of the buckets after it; only
+    the last one's is exposed, so the last bucket is made the smallest while
+    every earlier gather still fits under the (larger) compute that follows it.
+    """
     n_buckets = max(1, min(n_buckets, len(costs)))
     total = sum(costs) or 1.0
-    bucket, acc, out = 0, 0.0, []
+    weights = [n_buckets - k for k in range(n_buckets)]
+    bounds, acc = [], 0.0
+    for w in weights:
+        acc += w
+        bounds.append(total * acc / sum(weights))
+    bucket, run, out = 0, 0.0, []
     for c in costs:
-        if acc >= total * (bucket + 1) / n_buckets and bucket < n_buckets - 1:
+        if run >= bounds[bucket] and bucket < n_buckets - 1:
             bucket += 1
         out.append(bucket)
-        acc += c
+        run += c
     return out
 
 
@@ -188,7 +198,7 @@ class _Branch:
 class ShardedMuonAdamW:
     """The MuonAdamW step partitioned over a process group (see the module docstring)."""
 
-    def __init__(self, adam_params, muon_params, muon_config, adam_config, process_group, *, n_buckets=4,
+    def __init__(self, adam_params, muon_params, muon_config, adam_config, process_group, *, n_buckets=5,
                  backend=None):
         if muon_config.adjust_lr_fn not in ADJUST_LR_FNS:
             raise AssertionError(f"Invalid adjust_lr_fn: {muon_config.adjust_lr_fn}")
@@ -267,16 +277,22 @@ class ShardedMuonAdamW:
         return dist.all_gather_into_tensor(flat, mine, group=self.pg, async_op=True)
 
     @torch.no_grad()
-    def step(self):
+    def step(self, wait_for=None):
+        """One sharded step.  ``wait_for`` (internal): callables run before the
+        AdamW launch (index 0) and before each Muon bucket (index 1 + bucket)."""
         ad, mu = self.adamw, self.muon
         ad.step_num += 1
         works = []
         bias1, bias2 = 1 - ad.beta1 ** ad.step_num, 1 - ad.beta2 ** ad.step_num
+        if wait_for:
+            wait_for[0]()
         if self.adam_shard:
             self.backend.adamw(self._adam_quads(), lr=ad.lr, beta1=ad.beta1, beta2=ad.beta2, eps=ad.eps,
                                weight_decay=ad.weight_decay, bias1=bias1, bias2=bias2, timer=ad._timer)
             works.append(self._gather(self.adam_flat, self.adam_shard))
         for b, seg in enumerate(self.seg_sizes):
+            if wait_for:
+                wait_for[1 + b]()
             self.backend.muon(b, self._bucket_triples(b), adjust_lr_fn=mu.adjust_lr_fn, beta=mu.beta,
                               nesterov=mu.is_nesterov, a=mu.a, b=mu.b, c=mu.c, ns_steps=mu.steps, eps=mu.eps,
                               lr=mu.lr, weight_decay=mu.weight_decay, timer=mu._timer)
@@ -284,6 +300,39 @@ class ShardedMuonAdamW:
                 works.append(self._gather(self.muon_flats[b], seg))
         for w in works:
             w.wait()
+
+    @torch.no_grad()
+    def step_from_host(self, host_grads):
+        """:meth:`step` with gradients in host memory: each rank copies only the
+        gradient pieces it reads, on a side stream, in the order the work
+        consumes them (AdamW shard, then bucket by bucket)."""
+        main = torch.cuda.current_stream()
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = torch.cuda.Stream(device=main.device)
+        copy = self._copy_stream
+        copy.wait_stream(main)
+        ad, mu = self.adamw, self.muon
+        for p in list(ad.model_params) + list(mu.model_params):
+            if p.grad is None and host_grads.get(p) is not None:
+                p.grad = torch.empty_like(p)
+        events = []
+        with torch.cuda.stream(copy):
+            for i, start, length, _ in self.adam_pieces:
+                p = ad.model_params[i]
+                h = host_grads.get(p)
+                if h is not None:
+                    p.grad.reshape(-1)[start:start + length].copy_(h.reshape(-1)[start:start + length],
+                                                                   non_blocking=True)
+            events.append(torch.cuda.Event())
+            events[-1].record(copy)
+            for b in range(len(self.seg_sizes)):
+                for p, s in zip(mu.model_params, self.slots):
+                    h = host_grads.get(p)
+                    if s.bucket == b and s.owner == self.rank and h is not None:
+                        p.grad.copy_(h, non_blocking=True)
+                events.append(torch.cuda.Event())
+                events[-1].record(copy)
+        self.step(wait_for=[lambda k=k: main.wait_event(events[k]) for k in range(len(events))])
 
     # ------------------------------------------------------------------ introspection
     def owned_muon_shapes(self):

@@ -158,9 +158,9 @@ class TritonMuon:
             self.momentum[param] = torch.zeros_like(param, device=param.device, dtype=param.dtype)
         self._plan = MuonPlan()
 
-    def _active(self):
+    def _active(self, only=None):
         triples = []
-        for p in self.model_params:
+        for p in (self.model_params if only is None else only):
             if p.grad is None:
                 continue
             if p.ndim != 2:

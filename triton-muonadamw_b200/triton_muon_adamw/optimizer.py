@@ -180,6 +180,67 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         self.adamw.step()
         self.muon.step()
 
+    @torch.no_grad()
+    def step_from_host(self, host_grads, n_buckets: int = 5) -> None:
+        """One step whose gradients live in (pinned) host memory.
+
+        ``host_grads`` maps each parameter to its host gradient (a dict keyed by
+        Parameter, or a sequence in the order ``param_group["adam"] +
+        param_group["muon"]``).  The result equals copying every gradient into
+        ``param.grad`` and calling :meth:`step`, but the host-to-device copies
+        run on a side stream in the order the work consumes them -- AdamW
+        first, then the Muon matrices in buckets of decreasing size -- so each
+        bucket's Newton-Schulz work overlaps the copies of the next.
+        """
+        params = list(self.param_group["adam"]) + list(self.param_group["muon"])
+        if not isinstance(host_grads, dict):
+            host_grads = dict(zip(params, host_grads))
+        if self.distributed is not None:
+            self.distributed.step_from_host(host_grads)
+            return
+        from .distributed import ns_cost, split_buckets  # noqa: PLC0415
+        from .muon.cuda_muon import MuonPlan, run_muon_plan  # noqa: PLC0415
+        main = torch.cuda.current_stream()
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = torch.cuda.Stream(device=main.device)
+            self._bucket_plans = {}
+        copy = self._copy_stream
+        copy.wait_stream(main)  # the previous step may still read the gradient buffers
+
+        for p in params:  # allocated on the main stream, which owns them afterwards
+            if p.grad is None and host_grads.get(p) is not None:
+                p.grad = torch.empty_like(p)
+
+        def upload(ps):
+            with torch.cuda.stream(copy):
+                for p in ps:
+                    h = host_grads.get(p)
+                    if h is not None:
+                        p.grad.copy_(h, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy)
+            return ev
+
+        main.wait_event(upload(self.adamw.model_params))
+        self.adamw.step()
+        mu = self.muon
+        mats = [p for p in mu.model_params if p in host_grads or p.grad is not None]
+        buckets = split_buckets([ns_cost(p.shape) for p in mats], n_buckets) if mats else []
+        groups = [[p for p, b in zip(mats, buckets) if b == k] for k in range(max(buckets) + 1 if buckets else 0)]
+        events = [upload(g) for g in groups]
+        for k, (g, ev) in enumerate(zip(groups, events)):
+            main.wait_event(ev)
+            triples = mu._active(only=g)
+            if not triples:
+                continue
+            plan = self._bucket_plans.setdefault(k, MuonPlan())
+            plan.ensure(triples, mu.adjust_lr_fn, triples[0][0].device)
+            run_muon_plan(plan, beta=mu.beta, nesterov=mu.is_nesterov, a=mu.a, b=mu.b, c=mu.c, ns_steps=mu.steps,
+                          eps=mu.eps, lr=mu.lr, weight_decay=mu.weight_decay)
+        for p in params:
+            if p.grad is not None:
+                p.grad.record_stream(copy)
+
     def zero_grad(self) -> None:
         """Reset the gradients of both branches to zero in place."""
         self.adamw.zero_grad()
@@ -189,7 +250,10 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         """Error bits recorded by the Muon kernels since the last read (0 = healthy)."""
         if self.distributed is not None:
             return self.distributed.status()
-        return self.muon.device_status(clear)
+        st = self.muon.device_status(clear)
+        for plan in getattr(self, "_bucket_plans", {}).values():
+            st |= plan.read_status(clear)
+        return st
 
     # -- checkpointing -----------------------------------------------------
     def state_dict(self) -> dict[str, object]:
