@@ -207,6 +207,42 @@ __device__ __forceinline__ void chunk_prefetch(const GemmArgs& args, const MatDe
   for (int q = 0; q < 4; ++q) in.q[q] = s4[q];
 }
 
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Update kernels fetch the epilogue's X block with TMA instead of per-thread
+// loads: lane 0 loads the warp's 32 rows x 32 columns (2 KB, 64-byte swizzle)
+// into the second half of the warp's staging buffer (the half the mirror
+// block uses in the symmetric kernels).  Per-thread 16-byte loads of 32
+// different rows cost ~12% of tensor throughput per clock and, together with
+// the output stores, pushed the kernel into the power cap.
+__device__ __forceinline__ void in_issue(uint8_t* stage, uint64_t* bar, const CUtensorMap* map, int x, int y) {
+  if ((threadIdx.x & 31) == 0) {
+    mbar_arrive_expect_tx(bar, 2048);
+    tma_load_2d(stage + 2048, map, bar, x, y);
+  }
+}
+
+// Waits for the block and copies this lane's row (32 bf16) into registers;
+// after the warp-wide sync the buffer may be refilled.
+__device__ __forceinline__ void in_take(uint8_t* stage, uint64_t* bar, uint32_t& phase, uint4 (&q)[4],
+                                        unsigned int* status, volatile int* abort_flag) {
+  if (!mbar_wait(bar, phase, status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE)) *abort_flag = 1;
+  phase ^= 1u;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(stage + 2048);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) q[j] = ld_shared_v4(base + static_cast<uint32_t>(lane * 64 + 16 * (j ^ ((lane >> 1) & 3))));
+  // These generic-proxy reads must be ordered before the next TMA (async-proxy)
+  // write into the buffer, which lane 0 issues after the warp sync.
+  fence_proxy_async_smem();
+  __syncwarp();
+}
+
 __device__ __forceinline__ float bf16_at(const uint4 (&q)[4], int k) {
   const uint4& u = q[k >> 3];
   const uint32_t w = ((k >> 1) & 3) == 0 ? u.x : ((k >> 1) & 3) == 1 ? u.y : ((k >> 1) & 3) == 2 ? u.z : u.w;
@@ -345,13 +381,16 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
 
 // Eight epilogue warps: warp w reads TMEM lanes 32*(w%4).. (the hardware
 // rule) and columns [128*half, 128*half+128) of the tile, half = (w-2)/4.
-// The global inputs of the first chunk are fetched before waiting for the
+// The inputs of the first chunk are fetched before waiting for the
 // accumulator, and each later chunk's inputs and TMEM load are in flight
-// while the previous chunk is finished.
+// while the previous chunk is finished (update kernels: TMA into shared
+// memory; polynomial: registers).
 template <int MODE>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull, uint64_t* tempty,
-                                              uint32_t tmem_base, uint8_t* stage, uint32_t rank,
+                                              uint32_t tmem_base, uint8_t* stage, uint64_t* in_bar, uint32_t rank,
                                               volatile int* abort_flag) {
+  constexpr bool TMA_IN = is_update<MODE>();
+  uint32_t in_phase = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int half = (warp - 2) >> 2;
@@ -375,15 +414,20 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     if (nch > 4) nch = 4;
     if (!is_update<MODE>() && blk < rowblk) nch = 0;
     const bool mirror = !is_update<MODE>() && blk > rowblk;
-    // The parameter-writing update keeps one chunk of global inputs in flight, the others two.
-    constexpr bool PREFETCH_NEXT = MODE != UPDATE_LAST;
+    const bool warp_rows = grow0 < md.m;  // some of this warp's rows exist (warp-uniform)
+    const CUtensorMap* in_map = args.tmaps + md.tmap_base + TM_X0_ST + (args.iter & 1);
 
     if (lane == 0 && MODE != UPDATE_LAST) {
       const int st = MODE == GRAM ? TM_GRAM_ST : MODE == POLY ? TM_POLY_ST : TM_X0_ST + ((args.iter & 1) ^ 1);
       tma_acquire_desc(args.tmaps + md.tmap_base + st);
     }
+    if (lane == 0 && TMA_IN) tma_acquire_desc(in_map);
     ChunkIn in[2];
-    if (nch > 0 && row_ok) chunk_prefetch<MODE>(args, md, grow, col0, in[0]);
+    if (TMA_IN) {
+      if (nch > 0 && warp_rows) in_issue(stage, in_bar, in_map, col0, grow0);
+    } else if (nch > 0 && row_ok) {
+      chunk_prefetch<MODE>(args, md, grow, col0, in[0]);
+    }
     if (!mbar_wait(&tfull[acc_buf], acc_phase, args.status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE) || *abort_flag) {
       *abort_flag = 1;
       break;
@@ -398,11 +442,14 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
+      if (TMA_IN && c < nch && warp_rows) {
+        in_take(stage, in_bar, in_phase, in[c & 1].q, args.status, abort_flag);
+        if (c + 1 < nch) in_issue(stage, in_bar, in_map, col0 + 32 * (c + 1), grow0);
+      }
       if (c + 1 < nch) {
-        if (PREFETCH_NEXT && row_ok) chunk_prefetch<MODE>(args, md, grow, col0 + 32 * (c + 1), in[(c + 1) & 1]);
+        if (!TMA_IN && row_ok) chunk_prefetch<MODE>(args, md, grow, col0 + 32 * (c + 1), in[(c + 1) & 1]);
         tmem_ld32_issue(tbase + 32 * (c + 1), acc[(c + 1) & 1]);
       }
-      if (!PREFETCH_NEXT && c > 0 && c < nch && row_ok) chunk_prefetch<MODE>(args, md, grow, col0 + 32 * c, in[c & 1]);
       if (c < nch)
         chunk_finish<MODE>(args, md, grow0, grow, row_ok, col0 + 32 * c, mirror, acc[c & 1], in[c & 1], stage);
       if (c + 1 < nch) tmem_ld_wait(acc[(c + 1) & 1]);
@@ -411,6 +458,7 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive_cluster(tempty_leader[acc_buf]);
+    if (*abort_flag) break;
   }
   if (lane == 0) bulk_wait_all();  // every output store has landed before the CTA retires
 }
@@ -428,7 +476,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* epi_in = drain + 1;  // one per epilogue warp: TMA fills of its input block
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_in + EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -443,6 +492,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tempty[a], 2 * EPI_WARPS);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
+    for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&epi_in[w], 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -460,7 +510,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, abort_flag);
   } else {
-    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * STAGE_OUT_BYTES, rank, abort_flag);
+    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * STAGE_OUT_BYTES, &epi_in[warp - 2],
+                        rank, abort_flag);
   }
   __syncthreads();
   if (*abort_flag && threadIdx.x == 0) {
