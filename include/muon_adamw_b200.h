@@ -43,24 +43,31 @@ enum {
   MAD_ERR_DEVICE = 5       /* a kernel reported an error in its status word */
 };
 
+/* Element type of parameters, gradients and Muon momentum (the AdamW moments
+ * are always float32, as in the reference, triton_adam.py:128-130). */
+enum { MAD_DTYPE_F32 = 0, MAD_DTYPE_BF16 = 1 };
+
 /* Message describing the last failure on the calling thread ("" if none). */
 const char* mad_last_error(void);
 
-/* ABI version of this library. */
+/* ABI version of this library (2: dtype fields in mad_adamw_tensor and mad_muon_matrix). */
 int32_t mad_abi_version(void);
 
 /* ------------------------------------------------------------------ AdamW */
 
-/* One float32 tensor of the AdamW branch (flattened; any shape). */
+/* One tensor of the AdamW branch (flattened; any shape).  param and grad have
+ * type `dtype`; exp_avg and exp_avg_sq are float32.  bf16 parameters are
+ * updated in float32 and rounded once on the store. */
 typedef struct mad_adamw_tensor {
-  float* param;
-  const float* grad;
+  void* param;       /* element type: dtype */
+  const void* grad;  /* element type: dtype */
   float* exp_avg;
   float* exp_avg_sq;
   int64_t numel;
+  int32_t dtype; /* MAD_DTYPE_F32 or MAD_DTYPE_BF16 */
 } mad_adamw_tensor;
 
-/* One AdamW update of one tensor, in place (replaces solve_adamw_step,
+/* One AdamW update of one float32 tensor, in place (replaces solve_adamw_step,
  * triton_adam.py:66-103; same argument meaning).  bias1/bias2 are the host
  * bias corrections 1-beta^t. */
 int mad_adamw_step(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t numel, float lr,
@@ -82,14 +89,18 @@ int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float
 
 /* ------------------------------------------------------------------ Muon */
 
-/* One float32 Muon matrix (rows x cols, row-major, contiguous). */
+/* One Muon matrix (rows x cols, row-major, contiguous); param, grad and
+ * momentum all of type `dtype`.  With bf16 the momentum/Nesterov glue and the
+ * parameter update round to bf16 after every operation, as the reference's
+ * eager ops on bf16 tensors do (triton_muon.py:346-349, 370-372). */
 typedef struct mad_muon_matrix {
-  float* param;
-  const float* grad;
-  float* momentum;
+  void* param;       /* element type: dtype (also grad and momentum) */
+  const void* grad;
+  void* momentum;
   int64_t rows;
   int64_t cols;
   double lr_scale; /* shape adjustment: scaled_lr = float(lr * lr_scale) (triton_muon.py:424-431) */
+  int32_t dtype;   /* MAD_DTYPE_F32 or MAD_DTYPE_BF16 */
 } mad_muon_matrix;
 
 /* Sizes and launch counts of a Muon plan; filled by mad_muon_plan_size and

@@ -67,16 +67,21 @@ def adamw_update_(p, g, m, v, *, lr, beta1, beta2, eps, weight_decay, bias1, bia
     The kernel there receives its scalars as float32 and forms ``1-beta1``,
     ``1-beta2`` and ``1-lr*wd`` in float32; every operation below is one
     float32 rounding, in the kernel's order.
+
+    A bf16 parameter (and gradient) is read as float32, the arithmetic is the
+    same, and the new value is rounded to bf16 on the store; the moments stay
+    float32 (triton_adam.py:128-130 allocates them as float32).
     """
     f = torch.float32
     one = torch.tensor(1.0, dtype=f)
     b1, b2 = torch.tensor(beta1, dtype=f), torch.tensor(beta2, dtype=f)
     lr_f, wd_f = torch.tensor(lr, dtype=f), torch.tensor(weight_decay, dtype=f)
+    g = g.to(f)
     m_t = (b1 * m) + ((one - b1) * g)
     v_t = (b2 * v) + ((one - b2) * (g * g))
     m_c = m_t / torch.tensor(bias1, dtype=f)
     v_c = v_t / torch.tensor(bias2, dtype=f)
-    decayed = (one - lr_f * wd_f) * p
+    decayed = (one - lr_f * wd_f) * p.to(f)
     p.copy_(decayed - lr_f * (m_c / (torch.sqrt(v_c) + torch.tensor(eps, dtype=f))))
     m.copy_(m_t)
     v.copy_(v_t)
@@ -91,7 +96,8 @@ def adamw_bias_corrections(beta1: float, beta2: float, step: int) -> tuple[float
 # Muon branch  (triton_muon.py)
 # --------------------------------------------------------------------------
 
-def muon_momentum_(grad: torch.Tensor, mom: torch.Tensor, beta: float, nesterov: bool) -> torch.Tensor:
+def muon_momentum_(grad: torch.Tensor, mom: torch.Tensor, beta: float, nesterov: bool,
+                   cpu_torch_alpha: bool = False) -> torch.Tensor:
     """Momentum EMA in place on ``mom`` and the (optionally Nesterov) update.
 
     ``triton_muon.py:346``: ``momentum.mul_(beta).add_(grad, alpha=1-beta)``
@@ -100,14 +106,34 @@ def muon_momentum_(grad: torch.Tensor, mom: torch.Tensor, beta: float, nesterov:
     with ``alpha = 1-beta`` formed in double by Python.
     ``triton_muon.py:348-349``: Nesterov returns ``grad + beta*(mom - grad)``
     as a new tensor (three float32 roundings) and leaves the buffer alone.
+    With bf16 buffers every one of these eager ops rounds its result to bf16
+    (torch computes in float32 and rounds on the store), which is what happens
+    below through the tensors' dtype; the fused add rounds float32 first.
+
+    ``alpha`` is a float32 scalar, as in torch's CUDA ``add`` kernel (it
+    computes in float32 for bf16 tensors), which is where the reference runs.
+    torch's CPU kernel instead rounds ``alpha`` to the tensor dtype first;
+    ``cpu_torch_alpha=True`` reproduces that, to pin the other rounding points
+    bit for bit against goldens recorded on CPU.
     """
     f = torch.float32
-    scaled = mom * torch.tensor(beta, dtype=f)
+    fbeta = torch.tensor(beta, dtype=f)
+    scaled = (mom.to(f) * fbeta).to(mom.dtype)
     alpha = float(torch.tensor(1.0 - beta, dtype=f))
+    if cpu_torch_alpha:
+        alpha = float(torch.tensor(alpha, dtype=mom.dtype))
     mom.copy_((scaled.double() + alpha * grad.double()).to(f))
-    if nesterov:
-        return grad + torch.tensor(beta, dtype=f) * (mom - grad)
-    return mom.clone()
+    return muon_nesterov(grad, mom, beta) if nesterov else mom.clone()
+
+
+def muon_nesterov(grad: torch.Tensor, mom: torch.Tensor, beta: float) -> torch.Tensor:
+    """``grad + beta * (momentum - grad)`` (triton_muon.py:348-349), each op rounded to the tensors' dtype.
+
+    ``beta * t`` with a Python float multiplies in float32 by float32(beta)
+    (the scalar is never rounded to t's dtype), then rounds to t's dtype.
+    """
+    f = torch.float32
+    return grad + ((mom - grad).to(f) * torch.tensor(beta, dtype=f)).to(mom.dtype)
 
 
 def to_wide_bf16(u: torch.Tensor) -> tuple[torch.Tensor, bool]:
@@ -201,10 +227,15 @@ def scaled_lr(lr: float, shape, adjust_lr_fn: str) -> float:
 
 
 def muon_apply_(p: torch.Tensor, o: torch.Tensor, lr: float, weight_decay: float, slr: float) -> None:
-    """Decoupled decay then the scaled update, as two float32 subtractions (triton_muon.py:368-372)."""
+    """Decoupled decay then the scaled update, as two float32 subtractions (triton_muon.py:368-372).
+
+    Each product of a Python float and a tensor is formed in float32 with the
+    float32 scalar and rounded to the tensor's dtype, then subtracted; with
+    bf16 parameters the update ``out`` is bf16 as well.
+    """
     f = torch.float32
-    p.sub_(torch.tensor(lr * weight_decay, dtype=f) * p)
-    p.sub_(torch.tensor(slr, dtype=f) * o.to(f))
+    p.sub_((p.to(f) * torch.tensor(lr * weight_decay, dtype=f)).to(p.dtype))
+    p.sub_((o.to(p.dtype).to(f) * torch.tensor(slr, dtype=f)).to(p.dtype))
 
 
 def muon_matrix_step_(p, g, mom, *, lr, beta, nesterov, coeffs, ns_steps, eps, weight_decay,
@@ -250,7 +281,7 @@ def split_params(model=None, explicit=None):
 
 @dataclass
 class OracleMuonAdamW:
-    """CPU restatement of ``MuonAdamW`` (optimizer.py:70-175) over float32 tensors.
+    """CPU restatement of ``MuonAdamW`` (optimizer.py:70-175) over float32 or bf16 tensors.
 
     Holds its own copies of the parameters (``params_adam``/``params_muon``)
     and their gradients; ``step()`` is AdamW then Muon (optimizer.py:156-159).

@@ -14,6 +14,12 @@ It imports the reference package ``triton_muon_adamw`` from
 * ``triton_adamw.pt`` -- the reference ``TritonAdamW`` (triton_adam.py:106-161)
   executed by the Triton interpreter (``TRITON_INTERPRET=1``), including a
   parameter whose gradient is ``None`` (the branch-global step count).
+* ``triton_muon_glue.pt`` -- the reference ``TritonMuon.step`` (triton_muon.py:414-448)
+  and its ``muon_step`` eager code (momentum EMA, Nesterov, bf16 cast,
+  transpose, Frobenius normalisation, decay and update: :346-372), float32
+  and bf16 parameters, with the Newton-Schulz call (:313-325) replaced by a
+  recorder that returns its input: the X each step hands to Newton-Schulz,
+  the momentum and the parameters after each step.
 
 The reference's Newton-Schulz kernels (triton_muon.py:35-310) cannot run in the
 Triton 3.6 interpreter (no bf16 there), so no Triton Muon golden exists; the
@@ -51,15 +57,15 @@ def _ref_pkg():
     return R
 
 
-def _params(shapes, gen, std):
-    return [torch.nn.Parameter(torch.randn(s, generator=gen) * std) for s in shapes]
+def _params(shapes, gen, std, dtype=torch.float32):
+    return [torch.nn.Parameter((torch.randn(s, generator=gen) * std).to(dtype)) for s in shapes]
 
 
 def wrapper_case(R, name, adam_shapes, muon_shapes, *, steps, muon, adam, seed, grad_std=1e-3,
-                 param_std=0.02, zero_params=False):
+                 param_std=0.02, zero_params=False, dtype=torch.float32):
     gen = torch.Generator().manual_seed(seed)
-    adam_p = _params(adam_shapes, gen, param_std)
-    muon_p = _params(muon_shapes, gen, param_std)
+    adam_p = _params(adam_shapes, gen, param_std, dtype)
+    muon_p = _params(muon_shapes, gen, param_std, dtype)
     if zero_params:
         for p in muon_p:
             p.data.zero_()
@@ -70,7 +76,7 @@ def wrapper_case(R, name, adam_shapes, muon_shapes, *, steps, muon, adam, seed, 
     grads, after = [], []
     ggen = torch.Generator().manual_seed(seed + 1000)
     for _ in range(steps):
-        gs = [torch.randn(p.shape, generator=ggen) * grad_std for p in adam_p + muon_p]
+        gs = [(torch.randn(p.shape, generator=ggen) * grad_std).to(dtype) for p in adam_p + muon_p]
         for p, g in zip(adam_p + muon_p, gs):
             p.grad = g.clone()
         opt.step()
@@ -107,9 +113,48 @@ def triton_adamw_case(R):
     torch.save(dict(shapes=shapes, cfg=cfg, init=init, grads=grads, after=after), HERE / "triton_adamw.pt")
 
 
+def triton_muon_glue_case(R):
+    import triton_muon_adamw.muon.triton_muon as TM  # noqa: PLC0415
+    seen = []
+
+    def recorder(X, a, b, c, out):   # stands in for the Triton Newton-Schulz step
+        seen.append(X.detach().clone())
+        out.copy_(X)
+
+    real = TM.newton_shultz_step
+    TM.newton_shultz_step = recorder
+    cases = []
+    try:
+        shapes = [(33, 70), (70, 33), (64, 64), (5, 3)]
+        for dtype in (torch.float32, torch.bfloat16):
+            for nesterov in (True, False):
+                gen = torch.Generator().manual_seed(len(cases) + 40)
+                params = _params(shapes, gen, 0.02, dtype)
+                init = [p.detach().clone() for p in params]
+                opt = TM.TritonMuon(params, lr=2e-2, weight_decay=0.1, coeffs=MUON_TORCH["coeffs"],
+                                    nesterov=nesterov, beta=0.95, ns_steps=2, eps=1e-7)
+                grads, xs, moms, after = [], [], [], []
+                for _ in range(2):
+                    gs = [(torch.randn(p.shape, generator=gen) * 1e-2).to(dtype) for p in params]
+                    for p, g in zip(params, gs):
+                        p.grad = g.clone()
+                    seen.clear()
+                    opt.step()
+                    xs.append(seen[0::2])        # the first Newton-Schulz input of each matrix
+                    grads.append(gs)
+                    moms.append([opt.momentum[p].clone() for p in params])
+                    after.append([p.detach().clone() for p in params])
+                cases.append(dict(dtype=str(dtype), nesterov=nesterov, shapes=shapes, lr=2e-2, weight_decay=0.1,
+                                  beta=0.95, eps=1e-7, init=init, grads=grads, x=xs, momentum=moms, after=after))
+    finally:
+        TM.newton_shultz_step = real
+    torch.save(cases, HERE / "triton_muon_glue.pt")
+
+
 def main():
     R = _ref_pkg()
     triton_adamw_case(R)
+    triton_muon_glue_case(R)
     # A tiny GPT with the C1 layout (tied embedding), two steps.
     a, m = gpt_c1_shapes(d=32, layers=2, ffn=128, vocab=256)
     wrapper_case(R, "gpt_tiny", a, m, steps=2, muon=MUON_TORCH, adam=ADAM_C1, seed=0)
@@ -123,6 +168,9 @@ def main():
                  muon=dict(MUON_TORCH, lr=1.0, weight_decay=0.0), adam=ADAM_C1, seed=5, zero_params=True)
     wrapper_case(R, "match_rms", [(16,)], [(48, 80), (80, 48)], steps=2,
                  muon=dict(MUON_TORCH, adjust_lr_fn="match_rms_adamw"), adam=ADAM_C1, seed=9)
+    # bf16 parameters: the wrapper keeps its AdamW moments in bf16, the Triton path in fp32.
+    a, m = gpt_c1_shapes(d=32, layers=1, ffn=128, vocab=128)
+    wrapper_case(R, "bf16", a, m + [(96, 40)], steps=2, muon=MUON_TORCH, adam=ADAM_C1, seed=11, dtype=torch.bfloat16)
     print("wrote", sorted(p.name for p in HERE.glob("*.pt")))
 
 

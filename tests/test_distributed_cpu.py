@@ -44,17 +44,17 @@ class OracleBackend:
                               eps=eps, weight_decay=weight_decay, adjust_lr_fn=adjust_lr_fn)
 
 
-def _make(seed=0):
+def _make(seed=0, dtype=torch.float32):
     gen = torch.Generator().manual_seed(seed)
-    adam = [torch.nn.Parameter(torch.randn(s, generator=gen) * 0.02) for s in ADAM_SHAPES]
-    muon = [torch.nn.Parameter(torch.randn(s, generator=gen) * 0.02) for s in MUON_SHAPES]
+    adam = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(dtype)) for s in ADAM_SHAPES]
+    muon = [torch.nn.Parameter((torch.randn(s, generator=gen) * 0.02).to(dtype)) for s in MUON_SHAPES]
     return adam, muon
 
 
-def _grads(step):
+def _grads(step, dtype=torch.float32):
     gen = torch.Generator().manual_seed(100 + step)
-    return ([torch.randn(s, generator=gen) * 1e-2 for s in ADAM_SHAPES],
-            [torch.randn(s, generator=gen) * 1e-2 for s in MUON_SHAPES])
+    return ([(torch.randn(s, generator=gen) * 1e-2).to(dtype) for s in ADAM_SHAPES],
+            [(torch.randn(s, generator=gen) * 1e-2).to(dtype) for s in MUON_SHAPES])
 
 
 def _free_port():
@@ -112,7 +112,8 @@ def _worker(rank, world, port, mode, q):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
         from triton_muon_adamw import AdamConfig, MuonConfig
         from triton_muon_adamw.distributed import ShardedMuonAdamW
-        adam, muon = _make()
+        dtype = torch.bfloat16 if mode == "bf16" else torch.float32
+        adam, muon = _make(dtype=dtype)
         ref = OracleMuonAdamW([p.detach().clone() for p in adam], [p.detach().clone() for p in muon],
                               adam=ADAM, muon=MUON)
         opt = ShardedMuonAdamW(adam, muon, MuonConfig(**MUON), AdamConfig(**ADAM), dist.group.WORLD, n_buckets=2,
@@ -120,13 +121,13 @@ def _worker(rank, world, port, mode, q):
         if mode == "die" and rank == 1:
             raise SystemExit(0)     # leaves before the first collective
         for step in range(2):
-            ga, gm = _grads(step)
+            ga, gm = _grads(step, dtype)
             for p, g in zip(adam + muon, ga + gm):
                 p.grad = g.clone()
             opt.step()
             ref.step(ga, gm)
         for p, r in zip(adam + muon, ref.params_adam + ref.params_muon):
-            assert torch.equal(p.detach(), r), f"rank {rank}: parameter {tuple(p.shape)} differs"
+            assert p.dtype == dtype and torch.equal(p.detach(), r), f"rank {rank}: parameter {tuple(p.shape)} differs"
         sd = opt.state_dict()
         for i, (m, v) in enumerate(zip(ref.exp_avg, ref.exp_avg_sq)):
             assert torch.equal(sd["adam"]["state"][i]["exp_avg"], m)
@@ -172,6 +173,12 @@ def _run(world, mode):
 def test_sharded_step_matches_single_process_oracle(world):
     out = _run(world, "normal")
     assert out == {r: "ok" for r in range(world)}, out
+
+
+def test_sharded_step_bf16_parameters():
+    """bf16 parameters: bf16 flat buffers and momentum, float32 AdamW moment shards."""
+    out = _run(2, "bf16")
+    assert out == {0: "ok", 1: "ok"}, out
 
 
 def test_rank_that_leaves_surfaces_as_collective_error():

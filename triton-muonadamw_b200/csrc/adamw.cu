@@ -1,4 +1,6 @@
 // AdamW branch: one elementwise fp32 update of param, exp_avg, exp_avg_sq.
+// Parameters and gradients may be float32 or bf16 (moments always float32);
+// bf16 values are widened on load and rounded once, to nearest even, on store.
 //
 // Follows the reference kernel's formula (triton_adam.py:53-63):
 //   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g²
@@ -18,6 +20,7 @@
 #include <vector>
 
 #include "capi_common.h"
+#include "elem_io.cuh"
 #include "plan.cuh"
 
 namespace mad {
@@ -44,11 +47,13 @@ __device__ __forceinline__ void adam_vec(float4& p, const float4& g, float4& m, 
   adam_elem(p.w, g.w, m.w, v.w, s);
 }
 
-// One tile [off, off+len) of one tensor.  Full aligned tiles take the
+// One tile [off, off+len) of one tensor whose parameter and gradient have
+// element type T (the moments are float32).  Full aligned tiles take the
 // 16-loads-in-flight path; ragged or misaligned pieces take a generic loop.
+template <typename T>
 __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
-  float* __restrict__ p = e.p + off;
-  const float* __restrict__ g = e.g + off;
+  T* __restrict__ p = static_cast<T*>(e.p) + off;
+  const T* __restrict__ g = static_cast<const T*>(e.g) + off;
   float* __restrict__ m = e.m + off;
   float* __restrict__ v = e.v + off;
   const int t = threadIdx.x;
@@ -57,8 +62,8 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = i * ADAM_THREADS + t;
-      rp[i] = __ldcs(reinterpret_cast<const float4*>(p) + idx);
-      rg[i] = __ldcs(reinterpret_cast<const float4*>(g) + idx);
+      rp[i] = ld4(p, idx);
+      rg[i] = ld4(g, idx);
       rm[i] = __ldcs(reinterpret_cast<const float4*>(m) + idx);
       rv[i] = __ldcs(reinterpret_cast<const float4*>(v) + idx);
     }
@@ -66,7 +71,7 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
     for (int i = 0; i < 4; ++i) {
       adam_vec(rp[i], rg[i], rm[i], rv[i], s);
       const int idx = i * ADAM_THREADS + t;
-      __stcs(reinterpret_cast<float4*>(p) + idx, rp[i]);
+      st4(p, idx, rp[i]);
       __stcs(reinterpret_cast<float4*>(m) + idx, rm[i]);
       __stcs(reinterpret_cast<float4*>(v) + idx, rv[i]);
     }
@@ -74,22 +79,29 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
   }
   const int nvec = e.vec ? (len >> 2) : 0;
   for (int i = t; i < nvec; i += ADAM_THREADS) {
-    float4 a = __ldcs(reinterpret_cast<const float4*>(p) + i);
-    float4 b = __ldcs(reinterpret_cast<const float4*>(g) + i);
+    float4 a = ld4(p, i);
+    float4 b = ld4(g, i);
     float4 c = __ldcs(reinterpret_cast<const float4*>(m) + i);
     float4 d = __ldcs(reinterpret_cast<const float4*>(v) + i);
     adam_vec(a, b, c, d, s);
-    __stcs(reinterpret_cast<float4*>(p) + i, a);
+    st4(p, i, a);
     __stcs(reinterpret_cast<float4*>(m) + i, c);
     __stcs(reinterpret_cast<float4*>(v) + i, d);
   }
   for (int i = nvec * 4 + t; i < len; i += ADAM_THREADS) {
-    float a = p[i], c = m[i], d = v[i];
-    adam_elem(a, g[i], c, d, s);
-    p[i] = a;
+    float a = ld1(p, i), c = m[i], d = v[i];
+    adam_elem(a, ld1(g, i), c, d, s);
+    st1(p, i, a);
     m[i] = c;
     v[i] = d;
   }
+}
+
+__device__ __forceinline__ void adam_tile_any(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
+  if (e.dtype == 1)
+    adam_tile<__nv_bfloat16>(e, off, len, s);
+  else
+    adam_tile<float>(e, off, len, s);
 }
 
 __global__ void __launch_bounds__(ADAM_THREADS) adamw_multi_kernel(const AdamEntry* __restrict__ entries,
@@ -100,7 +112,7 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_multi_kernel(const AdamEnt
     const int64_t off = (tile - e.tile_begin) * ADAM_TILE;
     const int64_t rem = e.numel - off;
     const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
-    adam_tile(e, off, len, s);
+    adam_tile_any(e, off, len, s);
   }
 }
 
@@ -109,7 +121,7 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_single_kernel(AdamEntry e,
     const int64_t off = tile * ADAM_TILE;
     const int64_t rem = e.numel - off;
     const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
-    adam_tile(e, off, len, s);
+    adam_tile_any(e, off, len, s);
   }
 }
 
@@ -137,6 +149,14 @@ static int adam_grid(int64_t n_tiles) {
 }
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// 4-element vectors are legal when p, g (4 elements: 16 B float32, 8 B bf16)
+// and the float32 moments (16 B) are aligned for them.
+static inline int32_t vec_ok(const void* p, const void* g, const float* m, const float* v, int32_t dtype) {
+  const bool pg = dtype == MAD_DTYPE_BF16 ? aligned8(p) && aligned8(g) : aligned16(p) && aligned16(g);
+  return pg && aligned16(m) && aligned16(v);
+}
 
 // Table layout: int32 tile map [n_tiles] at offset 0, then the AdamEntry array
 // at the next 256-byte boundary.  Both offsets follow from n_tiles alone, so a
@@ -168,7 +188,8 @@ extern "C" int mad_adamw_step(float* param, const float* grad, float* exp_avg, f
   e.v = exp_avg_sq;
   e.numel = numel;
   e.tile_begin = 0;
-  e.vec = aligned16(param) && aligned16(grad) && aligned16(exp_avg) && aligned16(exp_avg_sq);
+  e.dtype = MAD_DTYPE_F32;
+  e.vec = vec_ok(param, grad, exp_avg, exp_avg_sq, MAD_DTYPE_F32);
   const int64_t n_tiles = (numel + ADAM_TILE - 1) / ADAM_TILE;
   adamw_single_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       e, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
@@ -200,6 +221,8 @@ extern "C" int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors
     if (t.numel < 0) return fail(MAD_ERR_INVALID, "mad_adamw_plan: negative numel");
     if (t.numel > 0 && (!t.param || !t.grad || !t.exp_avg || !t.exp_avg_sq))
       return fail(MAD_ERR_INVALID, "mad_adamw_plan: null pointer in tensor %d", i);
+    if (t.dtype != MAD_DTYPE_F32 && t.dtype != MAD_DTYPE_BF16)
+      return fail(MAD_ERR_INVALID, "mad_adamw_plan: tensor %d has unknown dtype %d", i, t.dtype);
     AdamEntry& e = entries[i];
     std::memset(&e, 0, sizeof(e));
     e.p = t.param;
@@ -208,7 +231,8 @@ extern "C" int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors
     e.v = t.exp_avg_sq;
     e.numel = t.numel;
     e.tile_begin = tiles;
-    e.vec = aligned16(t.param) && aligned16(t.grad) && aligned16(t.exp_avg) && aligned16(t.exp_avg_sq);
+    e.dtype = t.dtype;
+    e.vec = vec_ok(t.param, t.grad, t.exp_avg, t.exp_avg_sq, t.dtype);
     tiles += (t.numel + ADAM_TILE - 1) / ADAM_TILE;
   }
   if (tiles > INT32_MAX) return fail(MAD_ERR_INVALID, "mad_adamw_plan: too many tiles");

@@ -1,5 +1,5 @@
 // Muon prologue, one pass over every planned matrix (triton_muon.py:346-356):
-//   mom = beta*mom + (1-beta)*g              (buffer updated in place, fp32)
+//   mom = beta*mom + (1-beta)*g              (buffer updated in place, fp32 or bf16)
 //   u   = g + beta*(mom - g)  if nesterov    (the buffer itself is untouched)
 //   X   = bf16(u), transposed when rows > cols, so X is m x n with m <= n
 //   s   = 1 / max(bf16(||X||_F), bf16(eps))  (the reference's bf16 norm)
@@ -9,10 +9,12 @@
 // with a per-matrix arrival counter, which it resets) adds the partials in a
 // fixed order in double precision.
 //
-// Traffic per element: read g, mom (8 B), write mom (4 B) and X (2 B).
+// Traffic per element: read g, mom (8 B), write mom (4 B) and X (2 B) with
+// float32 buffers; 4 + 2 + 2 B with bf16 buffers.
 #include <cuda_runtime.h>
 
 #include "capi_common.h"
+#include "elem_io.cuh"
 #include "plan.cuh"
 #include "ptx_sm100.cuh"
 
@@ -27,9 +29,63 @@ struct PrepScalars {
 
 // mom.mul_(beta).add_(grad, alpha=1-beta) (triton_muon.py:346): one rounded
 // product, then torch's fused `self + alpha*other` (a single FMA rounding).
+// With bf16 buffers each eager op's float32 result is rounded to bf16 on its
+// store, and so is each step of the Nesterov expression (triton_muon.py:348).
+template <bool BF16>
 __device__ __forceinline__ float prep_update(float g, float& mom, const PrepScalars& s) {
+  if (BF16) {
+    mom = bf16_round(__fmaf_rn(s.one_m_beta, g, bf16_round(__fmul_rn(mom, s.beta))));
+    if (!s.nesterov) return mom;
+    return bf16_round(__fadd_rn(g, bf16_round(__fmul_rn(s.beta, bf16_round(__fsub_rn(mom, g))))));
+  }
   mom = __fmaf_rn(s.one_m_beta, g, __fmul_rn(mom, s.beta));
   return s.nesterov ? __fadd_rn(g, __fmul_rn(s.beta, __fsub_rn(mom, g))) : mom;
+}
+
+// Momentum update of one 64x64 tile; xv receives the (Nesterov) update u for
+// the thread's 4 rows x 4 consecutive columns, 0 outside the matrix.
+template <typename T>
+__device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, bool full, float (&xv)[4][4],
+                                            const PrepScalars& s) {
+  constexpr bool BF16 = sizeof(T) == 2;
+  const int rows = md->rows, cols = md->cols, t = threadIdx.x;
+  const T* __restrict__ g = static_cast<const T*>(md->g);
+  T* __restrict__ mom = static_cast<T*>(md->mom);
+  const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
+  if (full) {
+    // All loads of the tile first (8 vectors in flight per thread), then compute and store.
+    float4 gv[4], mv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+      gv[i] = ld4(g + off, 0);
+      mv[i] = ld4(mom + off, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+      xv[i][0] = prep_update<BF16>(gv[i].x, mv[i].x, s);
+      xv[i][1] = prep_update<BF16>(gv[i].y, mv[i].y, s);
+      xv[i][2] = prep_update<BF16>(gv[i].z, mv[i].z, s);
+      xv[i][3] = prep_update<BF16>(gv[i].w, mv[i].w, s);
+      st4(mom + off, 0, mv[i]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + i * 16 + (t >> 4), c = c0 + cl;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      xv[i][k] = 0.f;
+      if (r < rows && c + k < cols) {
+        const int64_t off = static_cast<int64_t>(r) * cols + c + k;
+        float mvv = ld1(mom, off);
+        xv[i][k] = prep_update<BF16>(ld1(g, off), mvv, s);
+        st1(mom, off, mvv);
+      }
+    }
+  }
 }
 
 __global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __restrict__ mats,
@@ -50,48 +106,16 @@ __global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __rest
     const int local = static_cast<int>(tile - md->prep_begin);
     const int r0 = (local / md->prep_tiles_c) * PREP_TILE;
     const int c0 = (local % md->prep_tiles_c) * PREP_TILE;
-    const float* __restrict__ g = md->g;
-    float* __restrict__ mom = md->mom;
     __nv_bfloat16* __restrict__ x = md->x[0];
     const bool full = md->vec != 0 && r0 + PREP_TILE <= rows && c0 + PREP_TILE <= cols;
 
     float ss = 0.f;
     const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
     float xv[4][4];
-    if (full) {
-      // All loads of the tile first (8 x 16 B in flight per thread), then compute and store.
-      float4 gv[4], mv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
-        gv[i] = __ldcs(reinterpret_cast<const float4*>(g + off));
-        mv[i] = __ldcs(reinterpret_cast<const float4*>(mom + off));
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
-        xv[i][0] = prep_update(gv[i].x, mv[i].x, s);
-        xv[i][1] = prep_update(gv[i].y, mv[i].y, s);
-        xv[i][2] = prep_update(gv[i].z, mv[i].z, s);
-        xv[i][3] = prep_update(gv[i].w, mv[i].w, s);
-        __stcs(reinterpret_cast<float4*>(mom + off), mv[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = r0 + i * 16 + (t >> 4), c = c0 + cl;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          xv[i][k] = 0.f;
-          if (r < rows && c + k < cols) {
-            const int64_t off = static_cast<int64_t>(r) * cols + c + k;
-            float mvv = mom[off];
-            xv[i][k] = prep_update(g[off], mvv, s);
-            mom[off] = mvv;
-          }
-        }
-      }
-    }
+    if (md->dtype == 1)
+      prep_values<__nv_bfloat16>(md, r0, c0, full, xv, s);
+    else
+      prep_values<float>(md, r0, c0, full, xv, s);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int rl = i * 16 + (t >> 4);

@@ -11,8 +11,8 @@
 // s = 1/||X||_F on iteration 0 (prep writes X unnormalised) and 1 afterwards.
 // GRAM and POLY outputs are symmetric: only tiles touching the upper triangle
 // are computed, and every strictly-upper 128x128 block is also stored
-// transposed.  On the last iteration UPDATE writes the fp32 parameter instead
-// of X' (triton_muon.py:365-372): p -= (lr·wd)·p ; p -= scaled_lr·bf16(X'),
+// transposed.  On the last iteration UPDATE writes the parameter (float32 or
+// bf16) instead of X' (triton_muon.py:365-372): p -= (lr·wd)·p ; p -= scaled_lr·bf16(X'),
 // transposed back for tall matrices.
 //
 // CTA pairs (clusters of 2) compute 256 x 256 tiles with tcgen05.mma.cta_group::2:
@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 
 #include "capi_common.h"
+#include "elem_io.cuh"
 #include "plan.cuh"
 #include "ptx_sm100.cuh"
 
@@ -53,7 +54,7 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 
 
 enum Mode { GRAM = 0, POLY = 1, UPDATE = 2, UPDATE_LAST = 3 };
 
-// UPDATE_LAST is the update of the final iteration, which writes the fp32
+// UPDATE_LAST is the update of the final iteration, which writes the
 // parameters; it is a separate instantiation so the common path can keep two
 // chunks in flight without exceeding the register budget (168 per thread with
 // ten warps).
@@ -295,6 +296,74 @@ __device__ __forceinline__ void stage_and_store(uint8_t* stage, const float (&v)
   }
 }
 
+// p -= (lr*wd)*p ; p -= scaled_lr*o  (triton_muon.py:370-372): two float32
+// subtractions; with bf16 parameters every eager op's result is rounded to
+// bf16 (the products too, since `out` is then bf16).
+template <typename T>
+__device__ __forceinline__ float param_new(float p, float x, float slr, float lr_wd) {
+  const float o = bf16_round(x);
+  if (sizeof(T) == 2) {
+    const float w = bf16_round(__fsub_rn(p, bf16_round(__fmul_rn(lr_wd, p))));
+    return bf16_round(__fsub_rn(w, bf16_round(__fmul_rn(slr, o))));
+  }
+  return __fsub_rn(__fsub_rn(p, __fmul_rn(lr_wd, p)), __fmul_rn(slr, o));
+}
+
+// Parameter write of one epilogue row chunk (32 columns of X' row `grow`), in
+// pieces of CW columns (16 for float32, 8 for bf16, whose longer rounding
+// chain needs more registers): within a piece all loads are issued before any
+// store (a store could otherwise alias a later load and serialise the chunk).
+template <typename T>
+__device__ __forceinline__ void write_params(const MatDesc& md, const float (&v)[32], int grow, int gcol0, int m,
+                                             float slr, float lr_wd) {
+  constexpr int CW = sizeof(T) == 2 ? 8 : 16;
+  const int n = md.n;
+  T* __restrict__ p = static_cast<T*>(md.p);
+#pragma unroll
+  for (int h = 0; h < 32 / CW; ++h) {
+    const int c0 = gcol0 + CW * h;
+    float pv[CW];
+    if (!md.transposed) {
+      T* prow = p + static_cast<int64_t>(grow) * n + c0;
+      const bool vec = md.vec && c0 + CW <= n;
+      if (vec) {
+#pragma unroll
+        for (int q = 0; q < CW / 4; ++q) {
+          const float4 t = ld4(prow, q);
+          pv[4 * q] = t.x;
+          pv[4 * q + 1] = t.y;
+          pv[4 * q + 2] = t.z;
+          pv[4 * q + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < CW; ++k) pv[k] = (c0 + k < n) ? ld1(prow, k) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < CW; ++k) pv[k] = param_new<T>(pv[k], v[CW * h + k], slr, lr_wd);
+      if (vec) {
+#pragma unroll
+        for (int q = 0; q < CW / 4; ++q)
+          st4(prow, q, make_float4(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]));
+      } else {
+#pragma unroll
+        for (int k = 0; k < CW; ++k)
+          if (c0 + k < n) st1(prow, k, pv[k]);
+      }
+    } else {
+      // Parameter is n x m: X'[grow][col] lives at p[col][grow]; per k a warp touches 32 contiguous elements.
+      T* pcol = p + static_cast<int64_t>(c0) * m + grow;
+#pragma unroll
+      for (int k = 0; k < CW; ++k) pv[k] = (c0 + k < n) ? ld1(pcol, static_cast<int64_t>(k) * m) : 0.f;
+#pragma unroll
+      for (int k = 0; k < CW; ++k) pv[k] = param_new<T>(pv[k], v[CW * h + k], slr, lr_wd);
+#pragma unroll
+      for (int k = 0; k < CW; ++k)
+        if (c0 + k < n) st1(pcol, static_cast<int64_t>(k) * m, pv[k]);
+    }
+  }
+}
+
 template <int MODE>
 __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc& md, int grow0, int grow, bool row_ok,
                                              int gcol0, bool mirror, uint32_t (&acc)[32], const ChunkIn& in,
@@ -324,59 +393,12 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
     return;
   }
   if (!row_ok) return;
-  // Parameter write, in two halves of 16 columns: within a half all loads are
-  // issued before any store (a store could otherwise alias a later load and
-  // serialise the chunk).
-  // scaled_lr = lr * shape factor, formed in double and rounded once (triton_muon.py:424-431);
-  // p -= (lr*wd)*p ; p -= scaled_lr*o as two float32 subtractions (triton_muon.py:370-372).
-  const float slr = static_cast<float>(args.lr * md.lr_scale), lr_wd = args.lr_wd;
-  const int n = md.n;
-  float* __restrict__ p = md.p;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int c0 = gcol0 + 16 * h;
-    float pv[16];
-    if (!md.transposed) {
-      float* prow = p + static_cast<int64_t>(grow) * n + c0;
-      const bool vec = md.vec && c0 + 16 <= n;
-      if (vec) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 t = reinterpret_cast<const float4*>(prow)[q];
-          pv[4 * q] = t.x;
-          pv[4 * q + 1] = t.y;
-          pv[4 * q + 2] = t.z;
-          pv[4 * q + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 16; ++k) pv[k] = (c0 + k < n) ? prow[k] : 0.f;
-      }
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        pv[k] = __fsub_rn(__fsub_rn(pv[k], __fmul_rn(lr_wd, pv[k])), __fmul_rn(slr, bf16_round(v[16 * h + k])));
-      if (vec) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          reinterpret_cast<float4*>(prow)[q] = make_float4(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          if (c0 + k < n) prow[k] = pv[k];
-      }
-    } else {
-      // Parameter is n x m: X'[grow][col] lives at p[col][grow]; per k a warp touches 128 contiguous bytes.
-      float* pcol = p + static_cast<int64_t>(c0) * m + grow;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) pv[k] = (c0 + k < n) ? pcol[k * m] : 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        pv[k] = __fsub_rn(__fsub_rn(pv[k], __fmul_rn(lr_wd, pv[k])), __fmul_rn(slr, bf16_round(v[16 * h + k])));
-#pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (c0 + k < n) pcol[k * m] = pv[k];
-    }
-  }
+  // scaled_lr = lr * shape factor, formed in double and rounded once (triton_muon.py:424-431).
+  const float slr = static_cast<float>(args.lr * md.lr_scale);
+  if (md.dtype == 1)
+    write_params<__nv_bfloat16>(md, v, grow, gcol0, m, slr, args.lr_wd);
+  else
+    write_params<float>(md, v, grow, gcol0, m, slr, args.lr_wd);
 }
 
 // Eight epilogue warps: warp w reads TMEM lanes 32*(w%4).. (the hardware

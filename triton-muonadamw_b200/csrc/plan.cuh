@@ -14,17 +14,17 @@
 namespace mad {
 
 // ---------------------------------------------------------------- AdamW
-// One tensor of the multi-tensor AdamW launch.  `vec` is 1 when all four
-// pointers are 16-byte aligned, so whole float4 loads/stores are legal.
+// One tensor of the multi-tensor AdamW launch.  `vec` is 1 when every pointer
+// is 16-byte aligned, so 4-element vector loads/stores are legal.
 struct AdamEntry {
-  float* p;
-  const float* g;
+  void* p;             // parameter, element type `dtype`
+  const void* g;       // gradient, element type `dtype`
   float* m;
   float* v;
   int64_t numel;
   int64_t tile_begin;  // first global tile index of this tensor
   int32_t vec;
-  int32_t pad;
+  int32_t dtype;       // 0 float32, 1 bf16
 };
 static_assert(sizeof(AdamEntry) == 56, "AdamEntry layout");
 
@@ -48,9 +48,9 @@ constexpr int TMAPS_PER_MAT = 10;
 constexpr int PREP_TILE = 64;  // prep works on 64x64 tiles of the parameter
 
 struct MatDesc {
-  float* p;              // parameter, rows x cols, row-major fp32
-  const float* g;        // gradient, same layout
-  float* mom;            // momentum buffer, same layout
+  void* p;               // parameter, rows x cols, row-major, element type `dtype`
+  const void* g;         // gradient, same layout and type
+  void* mom;             // momentum buffer, same layout and type
   __nv_bfloat16* x[2];   // Newton-Schulz iterate, m x n (ld_x), ping-pong
   __nv_bfloat16* gram;   // A, m x m (ld_mm)
   __nv_bfloat16* poly;   // B, m x m (ld_mm)
@@ -65,8 +65,9 @@ struct MatDesc {
   int32_t prep_count;    // number of prep tiles
   uint32_t done;         // prep tiles finished this step (reset by the last one)
   int32_t tmap_base;     // index of this matrix's first tensor map
-  int32_t vec;           // p, g, mom 16-byte aligned and cols % 4 == 0
-  int32_t pad[2];
+  int32_t vec;           // p, g, mom 16-byte aligned and cols % (16 / element size) == 0
+  int32_t dtype;         // 0 float32, 1 bf16
+  int32_t pad;
 };
 static_assert(sizeof(MatDesc) == 128, "MatDesc layout");
 

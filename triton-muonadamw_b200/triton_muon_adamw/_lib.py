@@ -12,6 +12,8 @@ import os
 from pathlib import Path
 
 LIB_NAME = "libmuonadamw_b200.so"
+ABI_VERSION = 2  # mad_abi_version() of the library these structures describe
+DTYPE_F32, DTYPE_BF16 = 0, 1  # MAD_DTYPE_*
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 c_int32 = ctypes.c_int32
@@ -22,12 +24,12 @@ c_void_p = ctypes.c_void_p
 
 class AdamWTensor(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("exp_avg", c_void_p), ("exp_avg_sq", c_void_p),
-                ("numel", c_int64)]
+                ("numel", c_int64), ("dtype", c_int32)]
 
 
 class MuonMatrix(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("momentum", c_void_p), ("rows", c_int64),
-                ("cols", c_int64), ("lr_scale", ctypes.c_double)]
+                ("cols", c_int64), ("lr_scale", ctypes.c_double), ("dtype", c_int32)]
 
 
 class MuonPlanInfo(ctypes.Structure):
@@ -94,6 +96,10 @@ def load():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    version = lib.mad_abi_version()
+    if version != ABI_VERSION:
+        raise ImportError(f"{path} has ABI version {version}, these bindings need {ABI_VERSION}: rebuild it "
+                          "(python -m triton_muon_adamw._build)")
     _lib = lib
     return lib
 

@@ -3,7 +3,8 @@
 Replaces the reference's ``TritonAdamW`` (triton_adam.py:106-161), keeping
 its name, constructor, attributes (``model_params``, ``m``, ``v``,
 ``step_num``, ``lr``, ``beta1``, ``beta2``, ``weight_decay``, ``eps``) and
-behaviour: float32 ``exp_avg``/``exp_avg_sq`` allocated at construction, one
+behaviour: float32 or bf16 parameters (the gradient of the parameter's dtype),
+float32 ``exp_avg``/``exp_avg_sq`` allocated at construction, one
 branch-global step count for the bias corrections, parameters whose ``grad``
 is ``None`` skipped, ``zero_grad`` zeroing gradients in place.
 
@@ -23,17 +24,32 @@ import torch.nn as nn
 from .. import _lib
 
 
-def _check_tensor(p: torch.Tensor, what: str) -> None:
+DTYPE_CODES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def dtype_code(t: torch.Tensor, what: str) -> int:
+    """C-ABI element-type code of a parameter/gradient/momentum tensor."""
+    code = DTYPE_CODES.get(t.dtype)
+    if code is None:
+        raise TypeError(f"{what} must be float32 or bfloat16, got {t.dtype}")
+    return code
+
+
+def _check_tensor(p: torch.Tensor, what: str, dtype: torch.dtype | None = None) -> None:
     if not p.is_cuda:
         raise ValueError(f"{what} must be a CUDA tensor (this optimizer runs only on the GPU)")
-    if p.dtype != torch.float32:
-        raise TypeError(f"{what} must be float32, got {p.dtype}")
+    dtype_code(p, what)
+    if dtype is not None and p.dtype != dtype:
+        raise TypeError(f"{what} must have dtype {dtype}, got {p.dtype}")
     if not p.is_contiguous():
         raise ValueError(f"{what} must be contiguous")
 
 
 class AdamWTable:
-    """Device tile table over a list of (param, grad, exp_avg, exp_avg_sq) float32 views."""
+    """Device tile table over a list of (param, grad, exp_avg, exp_avg_sq) views.
+
+    param and grad share one dtype (float32 or bf16); the moments are float32.
+    """
 
     def __init__(self):
         self.key = None
@@ -42,13 +58,15 @@ class AdamWTable:
         self.numel = 0
 
     def ensure(self, quads, device) -> None:
-        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel()) for p, g, m, v in quads)
+        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), p.dtype)
+                    for p, g, m, v in quads)
         if key == self.key:
             return
         lib = _lib.load()
         arr = (_lib.AdamWTensor * max(1, len(quads)))()
         for i, (p, g, m, v) in enumerate(quads):
-            arr[i] = _lib.AdamWTensor(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel())
+            arr[i] = _lib.AdamWTensor(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(),
+                                      dtype_code(p, "AdamW parameter"))
         nbytes = ctypes.c_int64()
         _lib.check(lib.mad_adamw_table_bytes(arr, len(quads), ctypes.byref(nbytes)), "mad_adamw_table_bytes")
         self.table = torch.empty(max(1, nbytes.value), dtype=torch.uint8, device=device)
@@ -68,7 +86,7 @@ class AdamWTable:
 
 
 class TritonAdamW:
-    """AdamW over float32 CUDA parameters, one CUDA launch per step.
+    """AdamW over float32 or bf16 CUDA parameters, one CUDA launch per step.
 
     The name is the reference's (``triton_muon_adamw.adamw.TritonAdamW``) so
     imports keep working; there is no Triton code behind it.
@@ -102,7 +120,7 @@ class TritonAdamW:
             if p.grad is None:
                 continue
             _check_tensor(p, "AdamW parameter")
-            _check_tensor(p.grad, "AdamW gradient")
+            _check_tensor(p.grad, "AdamW gradient", p.dtype)
             quads.append((p.data, p.grad, self.m[p], self.v[p]))
         return quads
 

@@ -205,9 +205,12 @@ class ShardedMuonAdamW:
         for p in muon_params:
             if p.ndim != 2:
                 raise AssertionError("Muon only supports 2D tensors")
-        for p in list(adam_params) + list(muon_params):
-            if p.dtype != torch.float32:
-                raise TypeError(f"parameters must be float32, got {p.dtype}")
+        dtypes = {p.dtype for p in list(adam_params) + list(muon_params)}
+        if len(dtypes) > 1 or not dtypes <= {torch.float32, torch.bfloat16}:
+            raise TypeError(f"sharded parameters must all be float32 or all bfloat16, got {sorted(map(str, dtypes))}")
+        # Parameters and Muon momentum live in flat buffers of the parameters' dtype;
+        # the AdamW moments are float32.
+        self.dtype = dtypes.pop() if dtypes else torch.float32
         self.pg = process_group
         self.rank = dist.get_rank(process_group)
         self.world = dist.get_world_size(process_group)
@@ -226,7 +229,7 @@ class ShardedMuonAdamW:
         # AdamW: ZeRO-1 ranges over one flat buffer.
         self.adam_numels = [p.numel() for p in ad.model_params]
         self.adam_offsets, self.adam_shard, total = zero1_layout(self.adam_numels, self.world)
-        self.adam_flat = torch.zeros(total, dtype=torch.float32, device=self.device)
+        self.adam_flat = torch.zeros(total, dtype=self.dtype, device=self.device)
         _rehome(ad.model_params, self.adam_flat, self.adam_offsets)
         lo = self.rank * self.adam_shard
         self.adam_pieces = shard_pieces(self.adam_offsets, self.adam_numels, lo, lo + self.adam_shard)
@@ -236,7 +239,7 @@ class ShardedMuonAdamW:
         # Muon: owner segments per bucket.
         shapes = [tuple(p.shape) for p in mu.model_params]
         self.slots, self.seg_sizes = muon_layout(shapes, self.world, n_buckets)
-        self.muon_flats = [torch.zeros(self.world * seg, dtype=torch.float32, device=self.device)
+        self.muon_flats = [torch.zeros(self.world * seg, dtype=self.dtype, device=self.device)
                            for seg in self.seg_sizes]
         with torch.no_grad():
             for p, s in zip(mu.model_params, self.slots):
@@ -244,7 +247,7 @@ class ShardedMuonAdamW:
                 view.copy_(p.data)
                 p.data = view
         # Momentum for owned matrices, laid out like the owner's parameter segment.
-        self.mom_segs = [torch.zeros(seg, dtype=torch.float32, device=self.device) for seg in self.seg_sizes]
+        self.mom_segs = [torch.zeros(seg, dtype=self.dtype, device=self.device) for seg in self.seg_sizes]
         mu.momentum = {}
         for p, s in zip(mu.model_params, self.slots):
             if s.owner == self.rank:
@@ -372,7 +375,7 @@ class ShardedMuonAdamW:
                                  "exp_avg_sq": full_v[o:o + n].view_as(p).clone()}
         fulls = []
         for seg, mom in zip(self.seg_sizes, self.mom_segs):
-            f = torch.empty(seg * self.world, dtype=torch.float32, device=self.device)
+            f = torch.empty(seg * self.world, dtype=self.dtype, device=self.device)
             dist.all_gather_into_tensor(f, mom, group=self.pg)
             fulls.append(f)
         muon_state = {i: {"momentum_buffer": fulls[s.bucket][s.offset:s.offset + s.numel].view_as(p).clone()}

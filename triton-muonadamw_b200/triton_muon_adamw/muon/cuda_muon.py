@@ -25,6 +25,7 @@ import torch
 import torch.nn as nn
 
 from .. import _lib
+from ..adamw.cuda_adam import dtype_code
 
 ADJUST_LR_FNS = ("original", "match_rms_adamw", "spectral_unclamped")
 
@@ -44,7 +45,7 @@ def lr_scale(shape, adjust_lr_fn: str) -> float:
 
 
 class MuonPlan:
-    """Device plan for a fixed list of (param, grad, momentum) float32 matrices."""
+    """Device plan for a fixed list of (param, grad, momentum) matrices, each float32 or bf16."""
 
     def __init__(self):
         self.key = None
@@ -56,7 +57,8 @@ class MuonPlan:
         self.shapes = []
 
     def ensure(self, triples, adjust_lr_fn, device) -> None:
-        key = (adjust_lr_fn,) + tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), tuple(p.shape)) for p, g, m in triples)
+        key = (adjust_lr_fn,) + tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), tuple(p.shape), p.dtype)
+                                      for p, g, m in triples)
         if key == self.key:
             return
         lib = _lib.load()
@@ -64,7 +66,7 @@ class MuonPlan:
         arr = (_lib.MuonMatrix * max(1, n))()
         for i, (p, g, m) in enumerate(triples):
             arr[i] = _lib.MuonMatrix(p.data_ptr(), g.data_ptr(), m.data_ptr(), p.shape[0], p.shape[1],
-                                     lr_scale(p.shape, adjust_lr_fn))
+                                     lr_scale(p.shape, adjust_lr_fn), dtype_code(p, "Muon parameter"))
         info = _lib.MuonPlanInfo()
         _lib.check(lib.mad_muon_plan_size(arr, n, ctypes.byref(info)), "mad_muon_plan_size")
         self.table = torch.empty(max(1, info.table_bytes), dtype=torch.uint8, device=device)
@@ -122,7 +124,7 @@ def run_muon_plan(plan: MuonPlan, *, beta, nesterov, a, b, c, ns_steps, eps, lr,
 
 
 class TritonMuon:
-    """Muon over float32 CUDA matrices with hand-written sm_100a kernels.
+    """Muon over float32 or bf16 CUDA matrices with hand-written sm_100a kernels.
 
     The name is the reference's (``triton_muon_adamw.muon.TritonMuon``) so
     imports keep working; there is no Triton code behind it.
@@ -168,8 +170,9 @@ class TritonMuon:
             for t, what in ((p, "Muon parameter"), (p.grad, "Muon gradient"), (self.momentum[p], "Muon momentum")):
                 if not t.is_cuda:
                     raise ValueError(f"{what} must be a CUDA tensor (this optimizer runs only on the GPU)")
-                if t.dtype != torch.float32:
-                    raise TypeError(f"{what} must be float32, got {t.dtype}")
+                dtype_code(t, what)
+                if t.dtype != p.dtype:
+                    raise TypeError(f"{what} must have the parameter's dtype {p.dtype}, got {t.dtype}")
                 if not t.is_contiguous():
                     raise ValueError(f"{what} must be contiguous")
             if p.numel() == 0:

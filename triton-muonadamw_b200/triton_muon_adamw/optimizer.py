@@ -124,8 +124,9 @@ class MuonAdamW(TritonMuon, TritonAdamW):
 
     Two-dimensional parameters are updated with Muon, except the input
     embedding and the output head; all other trainable parameters (biases,
-    norms, embeddings, heads) use AdamW.  Parameters must be float32,
-    contiguous CUDA tensors; there is no CPU implementation.
+    norms, embeddings, heads) use AdamW.  Parameters must be float32 or
+    bfloat16, contiguous CUDA tensors (gradients and Muon momentum in the
+    parameter's dtype, AdamW moments float32); there is no CPU implementation.
 
     Parameters
     ----------
