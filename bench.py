@@ -1,6 +1,6 @@
 """Benchmark: one full MuonAdamW optimizer step on the Llama-3-8B-shaped parameter set.
 
-    python bench.py [--gpus N --steps K --warmup W] [--config 8b|1b3|c1] [--impl ours|reference]
+    python bench.py [--gpus N --steps K --warmup W] [--config 8b|1b3|prof] [--impl ours|reference|reference-triton]
 
 A step is one ``MuonAdamW.step()`` (AdamW branch + Muon branch with ns_steps
 Newton-Schulz iterations) over the whole synthetic parameter set, already in
@@ -15,7 +15,10 @@ kernel family.  ``cpu_baseline`` times the reference's CPU path
 under oracle/) on a bounded sample and extrapolates to the full step.
 
 With ``--impl reference`` only that CPU measurement runs (rank 0), each step a
-bounded sample extrapolated to the full step.
+bounded sample extrapolated to the full step.  ``--impl reference-triton``
+times the reference's own Triton ``MuonAdamW`` (the unmodified package
+installed under ``baseline/_ref``) on this GPU with the same shapes and
+synthetic data (rank 0 only; the reference is single-GPU).
 """
 
 from __future__ import annotations
@@ -232,7 +235,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -247,6 +250,11 @@ def main():
         if rank != 0:
             return
         run_reference_arm(args, cfg, world)
+        return
+    if args.impl == "reference-triton":
+        if rank != 0:
+            return
+        run_reference_triton_arm(args, cfg, world, local_rank)
         return
 
     torch.cuda.set_device(local_rank)
@@ -474,6 +482,52 @@ def run_reference_arm(args, cfg, world):
             "cpu_baseline": {"value": round(ms, 1), "unit": "ms/step", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(ms, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_triton_arm(args, cfg, world, local_rank):
+    """The reference's own Triton MuonAdamW on this GPU: same shapes, data and hyperparameters as ours."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "triton_muon_adamw" / "optimizer.py").exists():
+        print(json.dumps({"impl": "reference-triton", "unavailable": "baseline/_ref holds no reference install"}))
+        return
+    ours = (ROOT / "triton-muonadamw_b200").resolve()
+    sys.path[:] = [p for p in sys.path if Path(p or ".").resolve() != ours]
+    sys.path.insert(0, str(ref))
+    import triton_muon_adamw as R  # noqa: PLC0415  (the reference package, not ours)
+    assert Path(R.__file__).resolve().is_relative_to(ref.resolve()), R.__file__
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    adam_shapes, muon_shapes = cfg["shapes"]()
+    model = ShapedParams(adam_shapes, muon_shapes, dev, seed=0)
+    ggen = torch.Generator(device=dev).manual_seed(1)
+    for p in model.parameters():
+        p.grad = torch.empty_like(p).normal_(0.0, 1e-3, generator=ggen)
+    opt = R.MuonAdamW(model, muon_config=R.MuonConfig(lr=1e-3, beta=0.95, eps=1e-7, weight_decay=0.1, coeffs=COEFFS,
+                                                      nesterov=True, ns_steps=args.ns_steps),
+                      adam_config=R.AdamConfig(**cfg["adam"]), parameter_split="auto")
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        opt.step()
+    end.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    line = {"metric": f"MuonAdamW ms/step ({cfg['name']})", "value": round(ms, 3), "unit": "ms/step",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) params, N(0,1e-3) grads; no dataset)", "impl": "reference-triton",
+            "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "ns_steps": args.ns_steps,
+                       "coeffs": list(COEFFS), "parallelism": "single-gpu",
+                       "muon_matrices": len(opt.muon.model_params), "adamw_tensors": len(opt.adamw.model_params),
+                       "source": "reference package, unmodified, from baseline/_ref"},
+            "clocks": clock_info}
     print(json.dumps(line), flush=True)
 
 
