@@ -50,8 +50,23 @@ enum { MAD_DTYPE_F32 = 0, MAD_DTYPE_BF16 = 1 };
 /* Message describing the last failure on the calling thread ("" if none). */
 const char* mad_last_error(void);
 
-/* ABI version of this library (2: dtype fields in mad_adamw_tensor and mad_muon_matrix). */
+/* ABI version of this library (2: dtype fields in mad_adamw_tensor and mad_muon_matrix;
+ * 3: gradient reduction over ranks, CUDA IPC buffers). */
 int32_t mad_abi_version(void);
+
+/* Data-parallel gradients summed over the ranks of one node (no counterpart in
+ * the single-GPU reference).  Every rank's gradient buffer is mapped into this
+ * process (mad_ipc_open); rank k's copy of a gradient element at address g is
+ * read at g + delta[k] bytes (delta[own rank] = 0).  The kernels sum the
+ * copies in rank order in float32, multiply by `scale` (1/n_ranks for the
+ * mean), round to the gradient's element type and use the result as the
+ * gradient: the reduce-scatter of the gradients fused into the step. */
+#define MAD_MAX_RANKS 8
+typedef struct mad_grad_reduce {
+  int32_t n_ranks; /* 1..MAD_MAX_RANKS */
+  float scale;
+  int64_t delta[MAD_MAX_RANKS];
+} mad_grad_reduce;
 
 /* ------------------------------------------------------------------ AdamW */
 
@@ -86,6 +101,11 @@ int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors, void* dev
  * TritonAdamW.step per-tensor loop, triton_adam.py:132-153). */
 int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2, float eps,
                          float weight_decay, float bias1, float bias2, void* stream);
+
+/* mad_adamw_step_multi with each gradient element summed over the ranks of `reduce`. */
+int mad_adamw_step_multi_reduce(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2,
+                                float eps, float weight_decay, float bias1, float bias2,
+                                const mad_grad_reduce* reduce, void* stream);
 
 /* ------------------------------------------------------------------ Muon */
 
@@ -147,6 +167,10 @@ int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* dev_table, 
 int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float eps,
                   void* stream);
 
+/* mad_muon_prep with each gradient element summed over the ranks of `reduce`. */
+int mad_muon_prep_reduce(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float eps,
+                         const mad_grad_reduce* reduce, void* stream);
+
 /* Newton-Schulz iteration `iter` (0-based), one launch each:
  *   gram:   A  = s² X Xᵀ          upper-triangle tiles, mirrored
  *   poly:   B  = b A + c A A      upper-triangle tiles, mirrored
@@ -164,6 +188,11 @@ int mad_ns_update(const mad_muon_plan_info* info, void* dev_table, int32_t iter,
 int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float a,
                         float b, float c, int32_t ns_steps, float eps, double lr, double weight_decay, void* stream);
 
+/* mad_muon_step_multi with the prep's gradient summed over the ranks of `reduce`. */
+int mad_muon_step_multi_reduce(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
+                               float a, float b, float c, int32_t ns_steps, float eps, double lr,
+                               double weight_decay, const mad_grad_reduce* reduce, void* stream);
+
 /* The Muon step of ONE matrix without any allocation (no counterpart in the
  * reference).  For callers that cannot allocate at step time -- code under a
  * custom or pre-sized allocator, or a foreign-language host with no allocator
@@ -178,6 +207,21 @@ int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double 
 int mad_muon_step_noalloc(float* param, const float* grad, float* momentum, int64_t rows, int64_t cols,
                           double lr_scale, double beta, int32_t nesterov, float a, float b, float c, int32_t ns_steps,
                           float eps, double lr, double weight_decay, void* stream);
+
+/* ------------------------------------------------------------------ peer buffers */
+
+/* Device memory the other processes of this node can map (CUDA IPC), for the
+ * gradient buffers mad_grad_reduce reads.  The only entry points that
+ * allocate.  mad_ipc_alloc: `bytes` of device memory on the current device
+ * (zeroed) and its MAD_IPC_HANDLE_BYTES-byte handle for the peers.
+ * mad_ipc_open: maps a peer's allocation (peer access enabled) and returns its
+ * address in this process.  Close every mapping (all ranks) before the owner
+ * frees its allocation. */
+#define MAD_IPC_HANDLE_BYTES 64
+int mad_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle);
+int mad_ipc_free(void* dev_ptr);
+int mad_ipc_open(const void* handle, void** peer_ptr);
+int mad_ipc_close(void* peer_ptr);
 
 /* Copies the plan's device status word to *status (synchronises `stream`)
  * and, if clear != 0, resets it.  Non-zero bits mean a kernel gave up

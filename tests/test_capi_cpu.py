@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in {HEADER.name} but not exported"
     assert set(declared) == set(_lib.SIGNATURES), "ctypes signatures must cover exactly the header"
-    assert lib.mad_abi_version() == 2
+    assert lib.mad_abi_version() == 3
 
 
 def test_invalid_arguments_fail_before_any_cuda_call():

@@ -29,17 +29,58 @@ MUON = dict(lr=1e-2, beta=0.95, eps=1e-7, weight_decay=0.1, coeffs=(3.4445, -4.7
 ADAM = dict(lr=3e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
 
 
+class CpuArena:
+    """The gradient arena of CPU ranks: a plain tensor; a reduction all-gathers every rank's arena."""
+
+    def __init__(self, nbytes, device, pg):
+        self.tensor = torch.zeros(nbytes, dtype=torch.uint8)
+        self.pg = pg
+
+    def spec(self, scale):
+        return (self, scale)
+
+    def close(self):
+        pass
+
+
+def reduced(g, copies, arena, scale):
+    """Every rank's copy of ``g`` (same arena offset), summed in rank order in float32, scaled, rounded."""
+    off = g.data_ptr() - arena.tensor.data_ptr()
+    nbytes = g.numel() * g.element_size()
+    acc = None
+    for c in copies:
+        t = c[off:off + nbytes].view(g.dtype).view(g.shape).float()
+        acc = t if acc is None else acc + t
+    return (acc * torch.tensor(scale, dtype=torch.float32)).to(g.dtype)
+
+
 class OracleBackend:
     """CPU arithmetic for the sharded step (test only)."""
 
-    def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None):
+    def grad_arena(self, nbytes, device, pg):
+        return CpuArena(nbytes, device, pg)
+
+    @staticmethod
+    def _gather(reduce):
+        arena, _ = reduce
+        copies = [torch.empty_like(arena.tensor) for _ in range(dist.get_world_size(arena.pg))]
+        dist.all_gather(copies, arena.tensor, group=arena.pg)
+        return copies
+
+    def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None, reduce=None):
+        copies = self._gather(reduce) if reduce is not None else None
         for p, g, m, v in quads:
+            if reduce is not None:
+                g = reduced(g, copies, *reduce)
             adamw_update_(p, g, m, v, lr=lr, beta1=beta1, beta2=beta2, eps=eps, weight_decay=weight_decay,
                           bias1=bias1, bias2=bias2)
 
     def muon(self, bucket, triples, *, adjust_lr_fn, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay,
-             timer=None):
+             timer=None, reduce=None):
+        copies = self._gather(reduce) if reduce is not None else None
         for p, g, mom in triples:
+            if reduce is not None:
+                g = reduced(g, copies, *reduce)
             muon_matrix_step_(p, g, mom, lr=lr, beta=beta, nesterov=nesterov, coeffs=(a, b, c), ns_steps=ns_steps,
                               eps=eps, weight_decay=weight_decay, adjust_lr_fn=adjust_lr_fn)
 
@@ -112,18 +153,33 @@ def _worker(rank, world, port, mode, q):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
         from triton_muon_adamw import AdamConfig, MuonConfig
         from triton_muon_adamw.distributed import ShardedMuonAdamW
-        dtype = torch.bfloat16 if mode == "bf16" else torch.float32
+        dtype = torch.bfloat16 if mode in ("bf16", "reduce_bf16") else torch.float32
+        reduce = mode.startswith("reduce")
         adam, muon = _make(dtype=dtype)
         ref = OracleMuonAdamW([p.detach().clone() for p in adam], [p.detach().clone() for p in muon],
                               adam=ADAM, muon=MUON)
         opt = ShardedMuonAdamW(adam, muon, MuonConfig(**MUON), AdamConfig(**ADAM), dist.group.WORLD, n_buckets=2,
-                               backend=OracleBackend())
+                               backend=OracleBackend(), reduce_grads="mean" if reduce else None)
         if mode == "die" and rank == 1:
             raise SystemExit(0)     # leaves before the first collective
         for step in range(2):
             ga, gm = _grads(step, dtype)
-            for p, g in zip(adam + muon, ga + gm):
-                p.grad = g.clone()
+            if reduce:
+                # Data-parallel: rank r holds its own gradients; the step uses their mean.
+                per_rank = [[(g.float() * (1 + 0.25 * r) + 1e-3 * r).to(dtype) for g in ga + gm]
+                            for r in range(world)]
+                mean = [(sum(per_rank[r][i].float() for r in range(world)) * torch.tensor(1.0 / world)).to(dtype)
+                        for i in range(len(ga + gm))]
+                mine = per_rank[rank]
+                for i, (p, g) in enumerate(zip(adam + muon, mine)):
+                    if step == 0 and i % 2 == 0:
+                        p.grad = g.clone()       # a gradient outside the arena: copied in at step()
+                    else:
+                        p.grad.copy_(g)          # in place, inside the arena
+                ga, gm = mean[:len(ga)], mean[len(ga):]
+            else:
+                for p, g in zip(adam + muon, ga + gm):
+                    p.grad = g.clone()
             opt.step()
             ref.step(ga, gm)
         for p, r in zip(adam + muon, ref.params_adam + ref.params_muon):
@@ -179,6 +235,14 @@ def test_sharded_step_bf16_parameters():
     """bf16 parameters: bf16 flat buffers and momentum, float32 AdamW moment shards."""
     out = _run(2, "bf16")
     assert out == {0: "ok", 1: "ok"}, out
+
+
+@pytest.mark.parametrize("world,mode", [(2, "reduce"), (3, "reduce"), (2, "reduce_bf16")])
+def test_sharded_step_reduces_per_rank_gradients(world, mode):
+    """reduce_grads="mean": each rank's own gradients, read from the gradient arenas of all ranks at the
+    owner's offsets, summed in rank order -- the result equals one step on the mean gradients."""
+    out = _run(world, mode)
+    assert out == {r: "ok" for r in range(world)}, out
 
 
 def test_rank_that_leaves_surfaces_as_collective_error():

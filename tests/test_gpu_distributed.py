@@ -36,6 +36,49 @@ def _grads(step, device):
     return [(torch.randn(s, generator=gen) * 1e-3).to(device) for s in ADAM_SHAPES + MUON_SHAPES]
 
 
+def _worker_reduce(rank, world, port, q, dtype):
+    """reduce_grads="mean": per-rank gradients read over NVLink vs one single-GPU step on their mean."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+        mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4, betas=(0.9, 0.95))
+        adam, muon = _params(dev)
+        adam, muon = ([torch.nn.Parameter(p.detach().to(dtype)) for p in ps] for ps in (adam, muon))
+        sharded = MuonAdamW({"adam": adam, "muon": muon}, muon_config=mc, adam_config=ac,
+                            parameter_split="explicit", process_group=dist.group.WORLD, reduce_grads="mean")
+        adam1, muon1 = _params(dev)
+        adam1, muon1 = ([torch.nn.Parameter(p.detach().to(dtype)) for p in ps] for ps in (adam1, muon1))
+        single = MuonAdamW({"adam": adam1, "muon": muon1}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+        for step in range(3):
+            base = _grads(step, dev)
+            per_rank = [[(g * (1 + 0.5 * r) + 1e-4 * r).to(dtype) for g in base] for r in range(world)]
+            for i, (p, g) in enumerate(zip(adam + muon, per_rank[rank])):
+                if step == 1 and i % 3 == 0:
+                    p.grad = g.clone()           # outside the shared buffer: copied in by step()
+                else:
+                    p.grad.copy_(g)
+            for i, p1 in enumerate(adam1 + muon1):
+                acc = per_rank[0][i].float()
+                for r in range(1, world):
+                    acc = acc + per_rank[r][i].float()
+                p1.grad = (acc * (1.0 / world)).to(dtype)
+            sharded.step()
+            single.step()
+        torch.cuda.synchronize()
+        for p, p1 in zip(adam + muon, adam1 + muon1):
+            assert torch.equal(p.detach(), p1.detach()), f"rank {rank}: {tuple(p.shape)} {dtype} differs"
+        assert sharded.device_status() == 0 and single.device_status() == 0
+        sharded.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
 def _worker(rank, world, port, q):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -72,15 +115,13 @@ def _worker(rank, world, port, q):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
 
 
-def test_two_gpu_sharded_step_is_bit_identical():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _spawn(target, world, *extra):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q, *extra)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -92,4 +133,20 @@ def test_two_gpu_sharded_step_is_bit_identical():
     while not q.empty():
         r, msg = q.get()
         out[r] = msg
+    return out
+
+
+def test_two_gpu_sharded_step_is_bit_identical():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _spawn(_worker, 2)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_two_gpu_fused_gradient_reduction(dtype):
+    """Each rank's own gradients, summed over NVLink inside the AdamW and Muon-prep kernels."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _spawn(_worker_reduce, 2, dtype)
     assert out == {0: "ok", 1: "ok"}, out

@@ -27,6 +27,7 @@ namespace mad {
 
 struct AdamScalars {
   float lr, beta1, beta2, one_m_beta1, one_m_beta2, eps, decay, bias1, bias2;
+  GradReduce red;  // red.n > 0: the gradient is the mean of every rank's copy (peer memory)
 };
 
 __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v, const AdamScalars& s) {
@@ -50,6 +51,36 @@ __device__ __forceinline__ void adam_vec(float4& p, const float4& g, float4& m, 
 // One tile [off, off+len) of one tensor whose parameter and gradient have
 // element type T (the moments are float32).  Full aligned tiles take the
 // 16-loads-in-flight path; ragged or misaligned pieces take a generic loop.
+// The tile with the gradient summed over ranks: one 4-element vector per
+// thread and pass, every rank's copy of it loaded before the first add.  The
+// remote reads cross NVLink, which bounds this path, not HBM.
+template <typename T>
+__device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
+  T* __restrict__ p = static_cast<T*>(e.p) + off;
+  const T* g = static_cast<const T*>(e.g) + off;
+  float* __restrict__ m = e.m + off;
+  float* __restrict__ v = e.v + off;
+  const int t = threadIdx.x;
+  const int nvec = e.vec ? (len >> 2) : 0;
+  for (int i = t; i < nvec; i += ADAM_THREADS) {
+    const float4 b = ld4_ranks(g, i, s.red);
+    float4 a = ld4(p, i);
+    float4 c = __ldcs(reinterpret_cast<const float4*>(m) + i);
+    float4 d = __ldcs(reinterpret_cast<const float4*>(v) + i);
+    adam_vec(a, b, c, d, s);
+    st4(p, i, a);
+    __stcs(reinterpret_cast<float4*>(m) + i, c);
+    __stcs(reinterpret_cast<float4*>(v) + i, d);
+  }
+  for (int i = nvec * 4 + t; i < len; i += ADAM_THREADS) {
+    float a = ld1(p, i), c = m[i], d = v[i];
+    adam_elem(a, ld1_ranks(g, i, s.red), c, d, s);
+    st1(p, i, a);
+    m[i] = c;
+    v[i] = d;
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
   T* __restrict__ p = static_cast<T*>(e.p) + off;
@@ -97,22 +128,32 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
   }
 }
 
+template <bool REDUCE>
 __device__ __forceinline__ void adam_tile_any(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
-  if (e.dtype == 1)
-    adam_tile<__nv_bfloat16>(e, off, len, s);
-  else
-    adam_tile<float>(e, off, len, s);
+  if (REDUCE) {
+    if (e.dtype == 1)
+      adam_tile_reduce<__nv_bfloat16>(e, off, len, s);
+    else
+      adam_tile_reduce<float>(e, off, len, s);
+  } else {
+    if (e.dtype == 1)
+      adam_tile<__nv_bfloat16>(e, off, len, s);
+    else
+      adam_tile<float>(e, off, len, s);
+  }
 }
 
-__global__ void __launch_bounds__(ADAM_THREADS) adamw_multi_kernel(const AdamEntry* __restrict__ entries,
-                                                                   const int32_t* __restrict__ tile_map,
-                                                                   int64_t n_tiles, AdamScalars s) {
+// REDUCE: the gradient summed over ranks (a separate instantiation, so the
+// local path keeps its register budget and occupancy).
+template <bool REDUCE>
+__global__ void __launch_bounds__(ADAM_THREADS) adamw_multi_kernel(
+    const AdamEntry* __restrict__ entries, const int32_t* __restrict__ tile_map, int64_t n_tiles, AdamScalars s) {
   for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
     const AdamEntry e = entries[tile_map[tile]];
     const int64_t off = (tile - e.tile_begin) * ADAM_TILE;
     const int64_t rem = e.numel - off;
     const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
-    adam_tile_any(e, off, len, s);
+    adam_tile_any<REDUCE>(e, off, len, s);
   }
 }
 
@@ -121,7 +162,7 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_single_kernel(AdamEntry e,
     const int64_t off = tile * ADAM_TILE;
     const int64_t rem = e.numel - off;
     const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
-    adam_tile_any(e, off, len, s);
+    adam_tile_any<false>(e, off, len, s);
   }
 }
 
@@ -129,6 +170,7 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_single_kernel(AdamEntry e,
 // 1-beta2 and 1-lr*wd in float32 (triton_adam.py:53-58); so do we.
 static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, float wd, float bias1, float bias2) {
   AdamScalars s;
+  std::memset(&s, 0, sizeof(s));
   volatile float lr_wd = lr * wd;  // one float32 rounding, never contracted into the subtraction
   s.lr = lr;
   s.beta1 = beta1;
@@ -255,18 +297,40 @@ extern "C" int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors
   return MAD_OK;
 }
 
-extern "C" int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2,
-                                    float eps, float weight_decay, float bias1, float bias2, void* stream) {
+static int adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2, float eps,
+                            float weight_decay, float bias1, float bias2, const mad_grad_reduce* reduce,
+                            void* stream, const char* who) {
   clear_error();
-  if (n_tiles < 0) return fail(MAD_ERR_INVALID, "mad_adamw_step_multi: negative tile count");
+  if (n_tiles < 0) return fail(MAD_ERR_INVALID, "%s: negative tile count", who);
   if (n_tiles == 0) return MAD_OK;
-  if (!dev_table) return fail(MAD_ERR_INVALID, "mad_adamw_step_multi: null table");
-  if (!(bias1 > 0.f) || !(bias2 > 0.f))
-    return fail(MAD_ERR_INVALID, "mad_adamw_step_multi: bias corrections must be > 0");
+  if (!dev_table) return fail(MAD_ERR_INVALID, "%s: null table", who);
+  if (!(bias1 > 0.f) || !(bias2 > 0.f)) return fail(MAD_ERR_INVALID, "%s: bias corrections must be > 0", who);
+  AdamScalars sc = make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2);
+  if (int rc = grad_reduce_from(reduce, &sc.red, who)) return rc;
   const uint8_t* base = static_cast<const uint8_t*>(dev_table);
   const int32_t* tile_map = reinterpret_cast<const int32_t*>(base);
   const AdamEntry* entries = reinterpret_cast<const AdamEntry*>(base + entries_offset(n_tiles));
-  adamw_multi_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      entries, tile_map, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (sc.red.n > 0)
+    adamw_multi_kernel<true><<<adam_grid(n_tiles), ADAM_THREADS, 0, st>>>(entries, tile_map, n_tiles, sc);
+  else
+    adamw_multi_kernel<false><<<adam_grid(n_tiles), ADAM_THREADS, 0, st>>>(entries, tile_map, n_tiles, sc);
   return check_launch("adamw_multi_kernel");
+}
+
+extern "C" int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2,
+                                    float eps, float weight_decay, float bias1, float bias2, void* stream) {
+  return adamw_step_multi(dev_table, n_tiles, lr, beta1, beta2, eps, weight_decay, bias1, bias2, nullptr, stream,
+                          "mad_adamw_step_multi");
+}
+
+extern "C" int mad_adamw_step_multi_reduce(const void* dev_table, int64_t n_tiles, float lr, float beta1,
+                                           float beta2, float eps, float weight_decay, float bias1, float bias2,
+                                           const mad_grad_reduce* reduce, void* stream) {
+  if (!reduce) {
+    clear_error();
+    return fail(MAD_ERR_INVALID, "mad_adamw_step_multi_reduce: null reduce descriptor");
+  }
+  return adamw_step_multi(dev_table, n_tiles, lr, beta1, beta2, eps, weight_decay, bias1, bias2, reduce, stream,
+                          "mad_adamw_step_multi_reduce");
 }

@@ -4,9 +4,12 @@
 
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 
+#include "elem_io.cuh"
 #include "muon_adamw_b200.h"  // include/ of the repository (-I)
 
 namespace mad {
@@ -33,6 +36,20 @@ inline int fail_cuda(const char* what) {
 inline int check_launch(const char* kernel) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MAD_ERR_CUDA, "launch of %s failed: %s", kernel, cudaGetErrorString(e));
+  return MAD_OK;
+}
+
+// Device form of a mad_grad_reduce (null: no reduction, the local gradient).
+inline int grad_reduce_from(const mad_grad_reduce* in, GradReduce* out, const char* who) {
+  static_assert(MAD_MAX_RANKS == MAX_RANKS, "rank limit of the C ABI and the kernels");
+  std::memset(out, 0, sizeof(*out));
+  if (!in) return MAD_OK;
+  if (in->n_ranks < 1 || in->n_ranks > MAX_RANKS)
+    return fail(MAD_ERR_INVALID, "%s: n_ranks %d outside 1..%d", who, in->n_ranks, MAX_RANKS);
+  if (!std::isfinite(in->scale)) return fail(MAD_ERR_INVALID, "%s: non-finite gradient scale", who);
+  out->n = in->n_ranks;
+  out->scale = in->scale;
+  for (int k = 0; k < in->n_ranks; ++k) out->delta[k] = in->delta[k];
   return MAD_OK;
 }
 

@@ -28,4 +28,76 @@ __device__ __forceinline__ float ld1(const __nv_bfloat16* p, int64_t i) { return
 __device__ __forceinline__ void st1(float* p, int64_t i, float v) { p[i] = v; }
 __device__ __forceinline__ void st1(__nv_bfloat16* p, int64_t i, float v) { p[i] = __float2bfloat16_rn(v); }
 
+// ------------------------------------------------------------ gradients summed over ranks
+// A data-parallel gradient read as the sum of every rank's copy: rank k's copy
+// of the element at address g lives at g + delta[k] bytes (peer memory mapped
+// into this process, delta 0 for this rank's own copy).  Summed in rank order
+// in float32, multiplied by `scale` (1/n for a mean), rounded to the gradient's
+// element type.  n == 0: the local gradient alone, unchanged.
+constexpr int MAX_RANKS = 8;
+
+struct GradReduce {
+  int32_t n;
+  float scale;
+  int64_t delta[MAX_RANKS];
+};
+
+// Loads of another rank's memory bypass L1 (ld.global.cg): the copy a peer
+// wrote is never served from a line this SM cached earlier.
+__device__ __forceinline__ float4 ld4_peer(const float* p, int64_t i) {
+  return __ldcg(reinterpret_cast<const float4*>(p) + i);
+}
+__device__ __forceinline__ float4 ld4_peer(const __nv_bfloat16* p, int64_t i) {
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p) + i);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xFFFF0000u));
+}
+__device__ __forceinline__ float ld1_peer(const float* p, int64_t i) { return __ldcg(p + i); }
+__device__ __forceinline__ float ld1_peer(const __nv_bfloat16* p, int64_t i) {
+  return __uint_as_float(static_cast<uint32_t>(__ldcg(reinterpret_cast<const unsigned short*>(p) + i)) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ const T* rank_copy(const T* g, int64_t delta) {
+  return reinterpret_cast<const T*>(reinterpret_cast<const char*>(g) + delta);
+}
+
+__device__ __forceinline__ float round_as(const float*, float x) { return x; }
+__device__ __forceinline__ float round_as(const __nv_bfloat16*, float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// All ranks' loads are issued before the first add (up to MAX_RANKS vectors in flight).
+template <typename T>
+__device__ __forceinline__ float4 ld4_ranks(const T* g, int64_t i, const GradReduce& r) {
+  float4 v[MAX_RANKS];
+#pragma unroll
+  for (int k = 0; k < MAX_RANKS; ++k)
+    if (k < r.n) v[k] = ld4_peer(rank_copy(g, r.delta[k]), i);
+  float4 a = v[0];
+#pragma unroll
+  for (int k = 1; k < MAX_RANKS; ++k)
+    if (k < r.n) {
+      a.x = __fadd_rn(a.x, v[k].x);
+      a.y = __fadd_rn(a.y, v[k].y);
+      a.z = __fadd_rn(a.z, v[k].z);
+      a.w = __fadd_rn(a.w, v[k].w);
+    }
+  return make_float4(round_as(g, __fmul_rn(a.x, r.scale)), round_as(g, __fmul_rn(a.y, r.scale)),
+                     round_as(g, __fmul_rn(a.z, r.scale)), round_as(g, __fmul_rn(a.w, r.scale)));
+}
+
+template <typename T>
+__device__ __forceinline__ float ld1_ranks(const T* g, int64_t i, const GradReduce& r) {
+  float v[MAX_RANKS];
+#pragma unroll
+  for (int k = 0; k < MAX_RANKS; ++k)
+    if (k < r.n) v[k] = ld1_peer(rank_copy(g, r.delta[k]), i);
+  float a = v[0];
+#pragma unroll
+  for (int k = 1; k < MAX_RANKS; ++k)
+    if (k < r.n) a = __fadd_rn(a, v[k]);
+  return round_as(g, __fmul_rn(a, r.scale));
+}
+
 }  // namespace mad

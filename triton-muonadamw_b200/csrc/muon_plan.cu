@@ -22,7 +22,7 @@
 namespace mad {
 
 int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, double beta,
-                     int nesterov, float eps, cudaStream_t stream);
+                     int nesterov, float eps, const GradReduce& red, cudaStream_t stream);
 int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, const TileRef* tiles, int64_t n_tiles,
                    int iter, int last, float a, float b, float c, double lr, float lr_wd, unsigned int* status,
                    cudaStream_t stream);
@@ -330,14 +330,30 @@ int check_args(const mad_muon_plan_info* info, void* table, const char* who) {
 
 }  // namespace
 
-extern "C" int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
-                             float eps, void* stream) {
+static int muon_prep(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float eps,
+                     const mad_grad_reduce* reduce, void* stream, const char* who) {
   clear_error();
-  if (int rc = check_args(info, dev_table, "mad_muon_prep")) return rc;
+  if (int rc = check_args(info, dev_table, who)) return rc;
+  GradReduce red;
+  if (int rc = grad_reduce_from(reduce, &red, who)) return rc;
   if (info->n_mats == 0) return MAD_OK;
   const Views v = views(info, dev_table);
-  return launch_muon_prep(v.mats, v.prep_map, v.partials, info->prep_tiles, beta, nesterov, eps,
+  return launch_muon_prep(v.mats, v.prep_map, v.partials, info->prep_tiles, beta, nesterov, eps, red,
                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mad_muon_prep(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
+                             float eps, void* stream) {
+  return muon_prep(info, dev_table, beta, nesterov, eps, nullptr, stream, "mad_muon_prep");
+}
+
+extern "C" int mad_muon_prep_reduce(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
+                                    float eps, const mad_grad_reduce* reduce, void* stream) {
+  if (!reduce) {
+    clear_error();
+    return fail(MAD_ERR_INVALID, "mad_muon_prep_reduce: null reduce descriptor");
+  }
+  return muon_prep(info, dev_table, beta, nesterov, eps, reduce, stream, "mad_muon_prep_reduce");
 }
 
 extern "C" int mad_ns_gram(const mad_muon_plan_info* info, void* dev_table, int32_t iter, void* stream) {
@@ -375,20 +391,39 @@ extern "C" int mad_ns_update(const mad_muon_plan_info* info, void* dev_table, in
                         v.status, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
-                                   float a, float b, float c, int32_t ns_steps, float eps, double lr,
-                                   double weight_decay, void* stream) {
+static int muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov, float a,
+                           float b, float c, int32_t ns_steps, float eps, double lr, double weight_decay,
+                           const mad_grad_reduce* reduce, void* stream, const char* who) {
   clear_error();
-  if (int rc = check_args(info, dev_table, "mad_muon_step_multi")) return rc;
-  if (ns_steps < 1) return fail(MAD_ERR_INVALID, "mad_muon_step_multi: ns_steps must be >= 1");
+  if (int rc = check_args(info, dev_table, who)) return rc;
+  if (ns_steps < 1) return fail(MAD_ERR_INVALID, "%s: ns_steps must be >= 1", who);
   if (info->n_mats == 0) return MAD_OK;
-  if (int rc = mad_muon_prep(info, dev_table, beta, nesterov, eps, stream)) return rc;
+  if (int rc = muon_prep(info, dev_table, beta, nesterov, eps, reduce, stream, who)) return rc;
   for (int32_t it = 0; it < ns_steps; ++it) {
     if (int rc = mad_ns_gram(info, dev_table, it, stream)) return rc;
     if (int rc = mad_ns_poly(info, dev_table, it, b, c, stream)) return rc;
     if (int rc = mad_ns_update(info, dev_table, it, it == ns_steps - 1, a, lr, weight_decay, stream)) return rc;
   }
   return MAD_OK;
+}
+
+extern "C" int mad_muon_step_multi(const mad_muon_plan_info* info, void* dev_table, double beta, int32_t nesterov,
+                                   float a, float b, float c, int32_t ns_steps, float eps, double lr,
+                                   double weight_decay, void* stream) {
+  return muon_step_multi(info, dev_table, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay, nullptr, stream,
+                         "mad_muon_step_multi");
+}
+
+extern "C" int mad_muon_step_multi_reduce(const mad_muon_plan_info* info, void* dev_table, double beta,
+                                          int32_t nesterov, float a, float b, float c, int32_t ns_steps, float eps,
+                                          double lr, double weight_decay, const mad_grad_reduce* reduce,
+                                          void* stream) {
+  if (!reduce) {
+    clear_error();
+    return fail(MAD_ERR_INVALID, "mad_muon_step_multi_reduce: null reduce descriptor");
+  }
+  return muon_step_multi(info, dev_table, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay, reduce, stream,
+                         "mad_muon_step_multi_reduce");
 }
 
 extern "C" int mad_muon_read_status(const mad_muon_plan_info* info, void* dev_table, uint32_t* status, int32_t clear,

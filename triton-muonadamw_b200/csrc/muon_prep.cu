@@ -10,7 +10,8 @@
 // fixed order in double precision.
 //
 // Traffic per element: read g, mom (8 B), write mom (4 B) and X (2 B) with
-// float32 buffers; 4 + 2 + 2 B with bf16 buffers.
+// float32 buffers; 4 + 2 + 2 B with bf16 buffers.  With a gradient reduction
+// the other ranks' gradient copies are read over NVLink as well.
 #include <cuda_runtime.h>
 
 #include "capi_common.h"
@@ -25,6 +26,7 @@ constexpr int PREP_THREADS = 256;
 struct PrepScalars {
   float beta, one_m_beta, eps_bf16;
   int nesterov;
+  GradReduce red;  // red.n > 0: the gradient is the mean of every rank's copy (peer memory)
 };
 
 // mom.mul_(beta).add_(grad, alpha=1-beta) (triton_muon.py:346): one rounded
@@ -44,7 +46,7 @@ __device__ __forceinline__ float prep_update(float g, float& mom, const PrepScal
 
 // Momentum update of one 64x64 tile; xv receives the (Nesterov) update u for
 // the thread's 4 rows x 4 consecutive columns, 0 outside the matrix.
-template <typename T>
+template <typename T, bool REDUCE>
 __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, bool full, float (&xv)[4][4],
                                             const PrepScalars& s) {
   constexpr bool BF16 = sizeof(T) == 2;
@@ -54,12 +56,22 @@ __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, b
   const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
   if (full) {
     // All loads of the tile first (8 vectors in flight per thread), then compute and store.
+    // Summed over ranks, each row's copies are in flight together, one row at a time.
     float4 gv[4], mv[4];
+    if (REDUCE) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
-      gv[i] = ld4(g + off, 0);
-      mv[i] = ld4(mom + off, 0);
+      for (int i = 0; i < 4; ++i) {
+        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+        mv[i] = ld4(mom + off, 0);
+        gv[i] = ld4_ranks(g + off, 0, s.red);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+        gv[i] = ld4(g + off, 0);
+        mv[i] = ld4(mom + off, 0);
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -81,14 +93,18 @@ __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, b
       if (r < rows && c + k < cols) {
         const int64_t off = static_cast<int64_t>(r) * cols + c + k;
         float mvv = ld1(mom, off);
-        xv[i][k] = prep_update<BF16>(ld1(g, off), mvv, s);
+        const float gg = REDUCE ? ld1_ranks(g, off, s.red) : ld1(g, off);
+        xv[i][k] = prep_update<BF16>(gg, mvv, s);
         st1(mom, off, mvv);
       }
     }
   }
 }
 
-__global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __restrict__ mats,
+// REDUCE: the gradient summed over ranks (a separate instantiation, so the
+// local path keeps its register budget and occupancy).
+template <bool REDUCE>
+__global__ void __launch_bounds__(PREP_THREADS, REDUCE ? 1 : 4) muon_prep_kernel(MatDesc* __restrict__ mats,
                                                                  const int32_t* __restrict__ prep_map,
                                                                  float* __restrict__ partials, int64_t n_tiles,
                                                                  PrepScalars s) {
@@ -113,9 +129,9 @@ __global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __rest
     const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
     float xv[4][4];
     if (md->dtype == 1)
-      prep_values<__nv_bfloat16>(md, r0, c0, full, xv, s);
+      prep_values<__nv_bfloat16, REDUCE>(md, r0, c0, full, xv, s);
     else
-      prep_values<float>(md, r0, c0, full, xv, s);
+      prep_values<float, REDUCE>(md, r0, c0, full, xv, s);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int rl = i * 16 + (t >> 4);
@@ -209,9 +225,10 @@ __global__ void __launch_bounds__(PREP_THREADS) muon_prep_kernel(MatDesc* __rest
 }
 
 int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, double beta,
-                     int nesterov, float eps, cudaStream_t stream) {
+                     int nesterov, float eps, const GradReduce& red, cudaStream_t stream) {
   if (n_tiles <= 0) return MAD_OK;
   PrepScalars s;
+  s.red = red;
   // The reference passes Python floats: beta is rounded to float32 by the
   // multiply, alpha = 1 - beta is formed in double and then rounded.
   s.beta = static_cast<float>(beta);
@@ -220,7 +237,10 @@ int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, in
   s.nesterov = nesterov ? 1 : 0;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
   const int grid = static_cast<int>(n_tiles < cap ? n_tiles : cap);
-  muon_prep_kernel<<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
+  if (red.n > 0)
+    muon_prep_kernel<true><<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
+  else
+    muon_prep_kernel<false><<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
   return check_launch("muon_prep_kernel");
 }
 

@@ -12,7 +12,7 @@ import os
 from pathlib import Path
 
 LIB_NAME = "libmuonadamw_b200.so"
-ABI_VERSION = 2  # mad_abi_version() of the library these structures describe
+ABI_VERSION = 3  # mad_abi_version() of the library these structures describe
 DTYPE_F32, DTYPE_BF16 = 0, 1  # MAD_DTYPE_*
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
@@ -45,6 +45,14 @@ class MuonBuffers(ctypes.Structure):
                 ("ld_x", c_int64), ("ld_mm", c_int64), ("transposed", c_int32)]
 
 
+MAX_RANKS = 8            # MAD_MAX_RANKS
+IPC_HANDLE_BYTES = 64    # MAD_IPC_HANDLE_BYTES
+
+
+class GradReduce(ctypes.Structure):
+    _fields_ = [("n_ranks", c_int32), ("scale", c_float), ("delta", c_int64 * MAX_RANKS)]
+
+
 # name -> (restype, argtypes); every entry point declared in include/muon_adamw_b200.h
 SIGNATURES = {
     "mad_last_error": (ctypes.c_char_p, []),
@@ -56,11 +64,15 @@ SIGNATURES = {
                                       ctypes.POINTER(c_int64), c_void_p]),
     "mad_adamw_step_multi": (ctypes.c_int, [c_void_p, c_int64, c_float, c_float, c_float, c_float, c_float, c_float,
                                             c_float, c_void_p]),
+    "mad_adamw_step_multi_reduce": (ctypes.c_int, [c_void_p, c_int64, c_float, c_float, c_float, c_float, c_float,
+                                                   c_float, c_float, ctypes.POINTER(GradReduce), c_void_p]),
     "mad_muon_plan_size": (ctypes.c_int, [ctypes.POINTER(MuonMatrix), c_int32, ctypes.POINTER(MuonPlanInfo)]),
     "mad_muon_plan": (ctypes.c_int, [ctypes.POINTER(MuonMatrix), c_int32, c_void_p, c_void_p,
                                      ctypes.POINTER(MuonPlanInfo), ctypes.POINTER(MuonBuffers), c_void_p]),
     "mad_muon_prep": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32, c_float,
                                      c_void_p]),
+    "mad_muon_prep_reduce": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32,
+                                            c_float, ctypes.POINTER(GradReduce), c_void_p]),
     "mad_ns_gram": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_int32, c_void_p]),
     "mad_ns_poly": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_int32, c_float, c_float, c_void_p]),
     "mad_ns_update": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, c_int32, c_int32, c_float,
@@ -68,11 +80,18 @@ SIGNATURES = {
     "mad_muon_step_multi": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32, c_float,
                                            c_float, c_float, c_int32, c_float, ctypes.c_double, ctypes.c_double,
                                            c_void_p]),
+    "mad_muon_step_multi_reduce": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.c_double, c_int32,
+                                                  c_float, c_float, c_float, c_int32, c_float, ctypes.c_double,
+                                                  ctypes.c_double, ctypes.POINTER(GradReduce), c_void_p]),
     "mad_muon_step_noalloc": (ctypes.c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, ctypes.c_double,
                                              ctypes.c_double, c_int32, c_float, c_float, c_float, c_int32, c_float,
                                              ctypes.c_double, ctypes.c_double, c_void_p]),
     "mad_muon_read_status": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.POINTER(ctypes.c_uint32),
                                             c_int32, c_void_p]),
+    "mad_ipc_alloc": (ctypes.c_int, [c_int64, ctypes.POINTER(c_void_p), c_void_p]),
+    "mad_ipc_free": (ctypes.c_int, [c_void_p]),
+    "mad_ipc_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "mad_ipc_close": (ctypes.c_int, [c_void_p]),
 }
 
 _lib = None

@@ -77,12 +77,19 @@ class AdamWTable:
         self.numel = sum(p.numel() for p, _, _, _ in quads)
         self.key = key
 
-    def launch(self, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2) -> None:
+    def launch(self, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, reduce=None) -> None:
+        """One launch over the table; ``reduce`` (a ``GradReduce``) sums each gradient over ranks."""
         if self.n_tiles == 0:
             return
         lib = _lib.load()
-        _lib.check(lib.mad_adamw_step_multi(self.table.data_ptr(), self.n_tiles, lr, beta1, beta2, eps, weight_decay,
-                                            bias1, bias2, _lib.stream_handle()), "mad_adamw_step_multi")
+        if reduce is None:
+            _lib.check(lib.mad_adamw_step_multi(self.table.data_ptr(), self.n_tiles, lr, beta1, beta2, eps,
+                                                weight_decay, bias1, bias2, _lib.stream_handle()),
+                       "mad_adamw_step_multi")
+        else:
+            _lib.check(lib.mad_adamw_step_multi_reduce(self.table.data_ptr(), self.n_tiles, lr, beta1, beta2, eps,
+                                                       weight_decay, bias1, bias2, ctypes.byref(reduce),
+                                                       _lib.stream_handle()), "mad_adamw_step_multi_reduce")
 
 
 class TritonAdamW:

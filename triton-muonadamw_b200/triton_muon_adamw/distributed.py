@@ -20,7 +20,14 @@ optimizer step needs, with one real exchange step:
   launches, so NCCL traffic over NVLink overlaps the remaining work.
 
 Gradients are expected to be identical on every rank already (data-parallel
-all-reduce upstream).  All ranks must call ``step()`` together.
+all-reduce upstream) -- unless ``reduce_grads`` is set: then each rank's
+gradients are its own, un-reduced, and live in a gradient arena shared over
+CUDA IPC (``peer.PeerArena``) laid out like the parameter flat buffers; the
+AdamW and Muon-prep kernels read every rank's copy of the elements they own
+over NVLink and use the mean (or sum).  That replaces the data-parallel
+all-reduce (2x the gradient bytes per rank) by the reduce-scatter volume
+(1x), fused into the optimizer's first kernels.  All ranks must call
+``step()`` together.
 
 The arithmetic is delegated to a backend: :class:`CudaBackend` (the CUDA
 kernels) by default.  Tests of the partitioning logic on CPU ranks (gloo)
@@ -157,23 +164,28 @@ class CudaBackend:
         self.adam_table = AdamWTable()
         self.plans = {}
 
-    def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None):
+    def grad_arena(self, nbytes: int, device, process_group):
+        """The gradient arena shared with the other ranks (CUDA IPC)."""
+        from .peer import PeerArena  # noqa: PLC0415
+        return PeerArena(nbytes, device, process_group)
+
+    def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None, reduce=None):
         if not quads:
             return
         self.adam_table.ensure(quads, quads[0][0].device)
         if timer is not None:
             timer.mark("adamw")
         self.adam_table.launch(lr=lr, beta1=beta1, beta2=beta2, eps=eps, weight_decay=weight_decay, bias1=bias1,
-                               bias2=bias2)
+                               bias2=bias2, reduce=reduce)
 
     def muon(self, bucket: int, triples, *, adjust_lr_fn, beta, nesterov, a, b, c, ns_steps, eps, lr,
-             weight_decay, timer=None):
+             weight_decay, timer=None, reduce=None):
         if not triples:
             return
         plan = self.plans.setdefault(bucket, MuonPlan())
         plan.ensure(triples, adjust_lr_fn, triples[0][0].device)
         run_muon_plan(plan, beta=beta, nesterov=nesterov, a=a, b=b, c=c, ns_steps=ns_steps, eps=eps, lr=lr,
-                      weight_decay=weight_decay, timer=timer)
+                      weight_decay=weight_decay, timer=timer, reduce=reduce)
 
     def status(self) -> int:
         st = 0
@@ -199,7 +211,9 @@ class ShardedMuonAdamW:
     """The MuonAdamW step partitioned over a process group (see the module docstring)."""
 
     def __init__(self, adam_params, muon_params, muon_config, adam_config, process_group, *, n_buckets=5,
-                 backend=None):
+                 backend=None, reduce_grads=None):
+        if reduce_grads not in (None, "mean", "sum"):
+            raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
         if muon_config.adjust_lr_fn not in ADJUST_LR_FNS:
             raise AssertionError(f"Invalid adjust_lr_fn: {muon_config.adjust_lr_fn}")
         for p in muon_params:
@@ -254,6 +268,60 @@ class ShardedMuonAdamW:
                 o = s.offset - self.rank * self.seg_sizes[s.bucket]
                 mu.momentum[p] = self.mom_segs[s.bucket][o:o + s.numel].view_as(p)
 
+        self.reduce_grads = reduce_grads
+        self.arena = None
+        self._grad_views = []
+        if reduce_grads is not None:
+            self._make_grad_arena()
+
+    # ------------------------------------------------------------------ gradient arena
+    def _make_grad_arena(self):
+        """Gradient views laid out like the parameter flats, in one arena every rank maps."""
+        es = torch.empty((), dtype=self.dtype).element_size()
+        ad, mu = self.adamw, self.muon
+        off = _round_up(len(self.adam_flat) * es, 256)
+        bucket_base = []
+        for seg in self.seg_sizes:
+            bucket_base.append(off)
+            off += _round_up(self.world * seg * es, 256)
+        self.arena = self.backend.grad_arena(off, self.device, self.pg)
+        raw = self.arena.tensor
+
+        def view(byte_off, p):
+            return raw[byte_off:byte_off + p.numel() * es].view(self.dtype).view(p.shape)
+
+        self._grad_views = [(p, view(o * es, p)) for p, o in zip(ad.model_params, self.adam_offsets)]
+        self._grad_views += [(p, view(bucket_base[s.bucket] + s.offset * es, p))
+                             for p, s in zip(mu.model_params, self.slots)]
+        for p, v in self._grad_views:
+            if p.grad is not None:
+                v.copy_(p.grad)
+            p.grad = v
+
+    def _bind_grads(self):
+        """Gradients produced outside the arena (e.g. after ``zero_grad(set_to_none=True)``) are copied in."""
+        with torch.no_grad():
+            for p, v in self._grad_views:
+                g = p.grad
+                if g is not None and g.data_ptr() != v.data_ptr():
+                    v.copy_(g)
+                    p.grad = v
+
+    def _rank_sync(self):
+        """Stream-ordered barrier: work after it starts once every rank's stream has reached it."""
+        if not hasattr(self, "_sync_flag"):
+            self._sync_flag = torch.zeros(1, device=self.device)
+        dist.all_reduce(self._sync_flag, group=self.pg)
+
+    def close(self):
+        """Release the gradient arena (collective; with ``reduce_grads``).  Gradients are set to None."""
+        if self.arena is not None:
+            for p, _ in self._grad_views:
+                p.grad = None
+            self._grad_views = []
+            self.arena.close()
+            self.arena = None
+
     # ------------------------------------------------------------------ step
     def _adam_quads(self):
         quads = []
@@ -287,28 +355,39 @@ class ShardedMuonAdamW:
         ad.step_num += 1
         works = []
         bias1, bias2 = 1 - ad.beta1 ** ad.step_num, 1 - ad.beta2 ** ad.step_num
+        red = None
+        if self.reduce_grads is not None:
+            if self.arena is None:
+                raise RuntimeError("the gradient arena was released (close()); this optimizer cannot step")
+            self._bind_grads()
+            red = self.arena.spec(1.0 / self.world if self.reduce_grads == "mean" else 1.0)
+            self._rank_sync()      # every rank's gradients are complete before any rank reads them
         if wait_for:
             wait_for[0]()
         if self.adam_shard:
             self.backend.adamw(self._adam_quads(), lr=ad.lr, beta1=ad.beta1, beta2=ad.beta2, eps=ad.eps,
-                               weight_decay=ad.weight_decay, bias1=bias1, bias2=bias2, timer=ad._timer)
+                               weight_decay=ad.weight_decay, bias1=bias1, bias2=bias2, timer=ad._timer, reduce=red)
             works.append(self._gather(self.adam_flat, self.adam_shard))
         for b, seg in enumerate(self.seg_sizes):
             if wait_for:
                 wait_for[1 + b]()
             self.backend.muon(b, self._bucket_triples(b), adjust_lr_fn=mu.adjust_lr_fn, beta=mu.beta,
                               nesterov=mu.is_nesterov, a=mu.a, b=mu.b, c=mu.c, ns_steps=mu.steps, eps=mu.eps,
-                              lr=mu.lr, weight_decay=mu.weight_decay, timer=mu._timer)
+                              lr=mu.lr, weight_decay=mu.weight_decay, timer=mu._timer, reduce=red)
             if seg:
                 works.append(self._gather(self.muon_flats[b], seg))
         for w in works:
             w.wait()
+        if red is not None:
+            self._rank_sync()      # no rank overwrites its gradients while another may still read them
 
     @torch.no_grad()
     def step_from_host(self, host_grads):
         """:meth:`step` with gradients in host memory: each rank copies only the
         gradient pieces it reads, on a side stream, in the order the work
         consumes them (AdamW shard, then bucket by bucket)."""
+        if self.reduce_grads is not None:
+            raise NotImplementedError("step_from_host takes reduced gradients; it does not combine with reduce_grads")
         main = torch.cuda.current_stream()
         if not hasattr(self, "_copy_stream"):
             self._copy_stream = torch.cuda.Stream(device=main.device)

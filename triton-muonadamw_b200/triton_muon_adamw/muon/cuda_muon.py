@@ -94,12 +94,13 @@ class MuonPlan:
 
 
 def run_muon_plan(plan: MuonPlan, *, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay, timer=None,
-                  stream=None) -> None:
+                  stream=None, reduce=None) -> None:
     """Launch the whole Muon branch for a plan on the current (or given) stream.
 
     Without a timer this is one C call (``mad_muon_step_multi``); with one,
     the same launches are issued phase by phase with a CUDA event between
-    them so each kernel can be timed on its launching stream.
+    them so each kernel can be timed on its launching stream.  ``reduce`` (a
+    ``GradReduce``) makes the prep sum each gradient over ranks.
     """
     if plan.n_mats == 0:
         return
@@ -107,11 +108,20 @@ def run_muon_plan(plan: MuonPlan, *, beta, nesterov, a, b, c, ns_steps, eps, lr,
     info, tab, st = ctypes.byref(plan.info), plan.table.data_ptr(), _lib.stream_handle(stream)
     nest = 1 if nesterov else 0
     if timer is None:
-        _lib.check(lib.mad_muon_step_multi(info, tab, beta, nest, a, b, c, ns_steps, eps, lr, weight_decay, st),
-                   "mad_muon_step_multi")
+        if reduce is None:
+            _lib.check(lib.mad_muon_step_multi(info, tab, beta, nest, a, b, c, ns_steps, eps, lr, weight_decay, st),
+                       "mad_muon_step_multi")
+        else:
+            _lib.check(lib.mad_muon_step_multi_reduce(info, tab, beta, nest, a, b, c, ns_steps, eps, lr,
+                                                      weight_decay, ctypes.byref(reduce), st),
+                       "mad_muon_step_multi_reduce")
         return
     timer.mark("prep")
-    _lib.check(lib.mad_muon_prep(info, tab, beta, nest, eps, st), "mad_muon_prep")
+    if reduce is None:
+        _lib.check(lib.mad_muon_prep(info, tab, beta, nest, eps, st), "mad_muon_prep")
+    else:
+        _lib.check(lib.mad_muon_prep_reduce(info, tab, beta, nest, eps, ctypes.byref(reduce), st),
+                   "mad_muon_prep_reduce")
     for it in range(ns_steps):
         timer.mark("gram")
         _lib.check(lib.mad_ns_gram(info, tab, it, st), "mad_ns_gram")

@@ -142,7 +142,19 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         Optional ``torch.distributed`` process group (NCCL).  With more than
         one rank, Muon matrices are owned whole by one rank each, AdamW state
         is sharded ZeRO-1 style, and the updated parameters are all-gathered.
-        Gradients are expected to be identical on every rank already.
+        Gradients are expected to be identical on every rank already, unless
+        ``reduce_grads`` is given.
+    reduce_grads:
+        ``None`` (default), ``"mean"`` or ``"sum"``: with a process group of
+        more than one rank, each rank's gradients are its own (data-parallel,
+        not yet reduced).  ``param.grad`` tensors are re-homed into a buffer
+        the other ranks map over CUDA IPC, and the step's first kernels read
+        every rank's copy of the elements they update over NVLink and use the
+        mean (or sum) -- the gradient reduce-scatter fused into the step, in
+        place of a data-parallel all-reduce.  Zero gradients in place
+        (:meth:`zero_grad`) to keep them in that buffer; gradients found
+        elsewhere at ``step()`` are copied in.  Call :meth:`close` on every
+        rank before the process group is destroyed.
     """
 
     def __init__(
@@ -152,13 +164,17 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         adam_config: AdamConfig = AdamConfig(),  # noqa: B008
         parameter_split: Literal["auto", "explicit"] = "auto",
         process_group=None,
+        reduce_grads: Literal["mean", "sum"] | None = None,
     ) -> None:
+        if reduce_grads not in (None, "mean", "sum"):
+            raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
         adam_params, muon_params = split_parameters(model_params, parameter_split)
         self.process_group = process_group
         self.distributed = None
         if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
             from .distributed import ShardedMuonAdamW  # noqa: PLC0415
-            self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group)
+            self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group,
+                                                reduce_grads=reduce_grads)
             self.adamw = self.distributed.adamw
             self.muon = self.distributed.muon
         else:
@@ -172,6 +188,11 @@ class MuonAdamW(TritonMuon, TritonAdamW):
             "adam": self.adamw.model_params,
             "muon": self.muon.model_params,
         }
+
+    def close(self) -> None:
+        """Release the resources shared with other ranks (collective with ``reduce_grads``; else a no-op)."""
+        if self.distributed is not None:
+            self.distributed.close()
 
     def step(self) -> None:
         """Apply one update with both branches: AdamW, then Muon (optimizer.py:156-159)."""
