@@ -239,6 +239,8 @@ def main():
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--grad-reduce", action="store_true",
+                    help="at N>1 also time the step with per-rank gradients reduced inside it (reduce_grads)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
 
@@ -364,6 +366,11 @@ def main():
     # End to end: this step's gradients from pinned host memory, result read back.
     e2e = run_e2e(opt, model, dev, args, barrier, world)
 
+    grad_reduce = None
+    if args.grad_reduce and world > 1:
+        del opt
+        grad_reduce = run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, cores, detail = cpu_sample(args.config, cfg["adam"], args.ns_steps)
@@ -384,6 +391,8 @@ def main():
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clock_info, "cpu_baseline": cpu,
         }
+        if grad_reduce is not None:
+            line["grad_reduce"] = grad_reduce
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -457,6 +466,66 @@ def run_e2e(opt, model, dev, args, barrier, world):
             "d2h_bytes_per_step": int(out.numel() * 4), "steps": steps,
             "what": "MuonAdamW.step_from_host (grads H2D from pinned memory, overlapped) + final-norm D2H, "
                     "device-timed"}
+
+
+def run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier):
+    """Data-parallel gradients, different on every rank: the step with the reduction fused into its
+    first kernels (reduce_grads="mean", peer reads over NVLink) vs an NCCL all-reduce of the same
+    gradient bytes, which a data-parallel step without it needs first."""
+    import gc  # noqa: PLC0415
+
+    from triton_muon_adamw import MuonAdamW  # noqa: PLC0415
+    for p in model.parameters():
+        p.grad = None
+    gc.collect()
+    torch.cuda.empty_cache()
+    opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg,
+                    reduce_grads="mean")
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    for p in model.parameters():
+        p.grad.normal_(0.0, 1e-3, generator=gen)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            fn()
+        end.record()
+        barrier()
+        t = torch.tensor([start.elapsed_time(end) / args.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    fused = timed(opt.step)
+    # Per-kernel split of the fused step (events between launches) and the NVLink read rate of the
+    # two kernels that sum the peers' copies.
+    timer = PhaseTimer()
+    opt_branch_timer(opt, timer)
+    barrier()
+    for _ in range(2):
+        opt.step()
+    barrier()
+    opt_branch_timer(opt, None)
+    phases = {k: sum(v) / 2 for k, v in timer.durations().items()}
+    es = torch.empty((), dtype=opt.distributed.dtype).element_size()
+    peer_bytes = {"adamw": adam_elems_local(opt) * (world - 1) * es,
+                  "prep": sum(math.prod(sh) for sh in owned_shapes(opt)) * (world - 1) * es}
+    peer = {k: {"ms_per_step": round(phases.get(k, 0.0), 3), "peer_bytes": int(b),
+                "peer_read_gbs": round(b / (phases[k] * 1e-3) / 1e9, 1) if phases.get(k) else None}
+            for k, b in peer_bytes.items()}
+    arena = opt.distributed.arena.tensor
+    grads = arena.view(opt.distributed.dtype)
+    allreduce = timed(lambda: dist.all_reduce(grads, op=dist.ReduceOp.AVG, group=pg))
+    opt.close()
+    return {"fused_step_ms": round(fused, 3), "nccl_allreduce_ms": round(allreduce, 3),
+            "gradient_bytes_per_rank": int(arena.numel()), "reduce_kernels": peer,
+            "gemm_ms_per_step": round(sum(phases.get(k, 0.0) for k in ("gram", "poly", "update")), 3),
+            "what": "step with per-rank gradients summed inside the AdamW/Muon-prep kernels (peer loads over "
+                    "NVLink) vs the NCCL all-reduce (AVG) of the same gradient bytes that a step on reduced "
+                    "gradients needs first; compare fused_step_ms with nccl_allreduce_ms + value"}
 
 
 def e2e_grad_tensors(opt, model):

@@ -51,9 +51,9 @@ __device__ __forceinline__ void adam_vec(float4& p, const float4& g, float4& m, 
 // One tile [off, off+len) of one tensor whose parameter and gradient have
 // element type T (the moments are float32).  Full aligned tiles take the
 // 16-loads-in-flight path; ragged or misaligned pieces take a generic loop.
-// The tile with the gradient summed over ranks: one 4-element vector per
-// thread and pass, every rank's copy of it loaded before the first add.  The
-// remote reads cross NVLink, which bounds this path, not HBM.
+// The tile with the gradient summed over ranks.  Full tiles: each thread's
+// four vectors of every rank's copy, two ranks (8 vectors) in flight at a
+// time, then p, m, v; the remote reads cross NVLink, which bounds this path.
 template <typename T>
 __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
   T* __restrict__ p = static_cast<T*>(e.p) + off;
@@ -61,6 +61,25 @@ __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off
   float* __restrict__ m = e.m + off;
   float* __restrict__ v = e.v + off;
   const int t = threadIdx.x;
+  if (e.vec && len == ADAM_TILE) {
+    int64_t offs[4];
+    float4 gv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) offs[j] = 4 * static_cast<int64_t>(j * ADAM_THREADS + t);
+    ld4_ranks_rows<T, 4>(g, offs, gv, s.red);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int idx = j * ADAM_THREADS + t;
+      float4 a = ld4(p, idx);
+      float4 c = __ldcs(reinterpret_cast<const float4*>(m) + idx);
+      float4 d = __ldcs(reinterpret_cast<const float4*>(v) + idx);
+      adam_vec(a, gv[j], c, d, s);
+      st4(p, idx, a);
+      __stcs(reinterpret_cast<float4*>(m) + idx, c);
+      __stcs(reinterpret_cast<float4*>(v) + idx, d);
+    }
+    return;
+  }
   const int nvec = e.vec ? (len >> 2) : 0;
   for (int i = t; i < nvec; i += ADAM_THREADS) {
     const float4 b = ld4_ranks(g, i, s.red);

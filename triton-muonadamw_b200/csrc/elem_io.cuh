@@ -87,6 +87,48 @@ __device__ __forceinline__ float4 ld4_ranks(const T* g, int64_t i, const GradRed
                      round_as(g, __fmul_rn(a.z, r.scale)), round_as(g, __fmul_rn(a.w, r.scale)));
 }
 
+__device__ __forceinline__ float4 add4(const float4& a, const float4& b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+// R vectors (at element offsets off[j] from g) summed over ranks, two ranks'
+// loads (2R vectors) in flight at a time: remote reads are latency-bound, so
+// the bytes in flight per thread set the NVLink throughput.  The sum starts
+// from -0.0, which leaves rank 0's value unchanged (-0 + x == x for every x),
+// so the result equals the plain rank-order sum.
+template <typename T, int R>
+__device__ __forceinline__ void ld4_ranks_rows(const T* g, const int64_t (&off)[R], float4 (&out)[R],
+                                               const GradReduce& r) {
+  float4 acc[R];
+#pragma unroll
+  for (int j = 0; j < R; ++j) acc[j] = make_float4(-0.f, -0.f, -0.f, -0.f);
+  int k = 0;
+  for (; k + 2 <= r.n; k += 2) {
+    const T* ga = rank_copy(g, r.delta[k]);
+    const T* gb = rank_copy(g, r.delta[k + 1]);
+    float4 a[R], b[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      a[j] = ld4_peer(ga + off[j], 0);
+      b[j] = ld4_peer(gb + off[j], 0);
+    }
+#pragma unroll
+    for (int j = 0; j < R; ++j) acc[j] = add4(add4(acc[j], a[j]), b[j]);
+  }
+  if (k < r.n) {
+    const T* ga = rank_copy(g, r.delta[k]);
+    float4 a[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) a[j] = ld4_peer(ga + off[j], 0);
+#pragma unroll
+    for (int j = 0; j < R; ++j) acc[j] = add4(acc[j], a[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+    out[j] = make_float4(round_as(g, __fmul_rn(acc[j].x, r.scale)), round_as(g, __fmul_rn(acc[j].y, r.scale)),
+                         round_as(g, __fmul_rn(acc[j].z, r.scale)), round_as(g, __fmul_rn(acc[j].w, r.scale)));
+}
+
 template <typename T>
 __device__ __forceinline__ float ld1_ranks(const T* g, int64_t i, const GradReduce& r) {
   float v[MAX_RANKS];

@@ -59,12 +59,13 @@ __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, b
     // Summed over ranks, each row's copies are in flight together, one row at a time.
     float4 gv[4], mv[4];
     if (REDUCE) {
+      int64_t offs[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int64_t off = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
-        mv[i] = ld4(mom + off, 0);
-        gv[i] = ld4_ranks(g + off, 0, s.red);
+        offs[i] = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
+        mv[i] = ld4(mom + offs[i], 0);
       }
+      ld4_ranks_rows<T, 4>(g, offs, gv, s.red);
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -104,7 +105,7 @@ __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, b
 // REDUCE: the gradient summed over ranks (a separate instantiation, so the
 // local path keeps its register budget and occupancy).
 template <bool REDUCE>
-__global__ void __launch_bounds__(PREP_THREADS, REDUCE ? 1 : 4) muon_prep_kernel(MatDesc* __restrict__ mats,
+__global__ void __launch_bounds__(PREP_THREADS, REDUCE ? 2 : 4) muon_prep_kernel(MatDesc* __restrict__ mats,
                                                                  const int32_t* __restrict__ prep_map,
                                                                  float* __restrict__ partials, int64_t n_tiles,
                                                                  PrepScalars s) {
