@@ -239,8 +239,8 @@ def main():
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--grad-reduce", action="store_true",
-                    help="at N>1 also time the step with per-rank gradients reduced inside it (reduce_grads)")
+    ap.add_argument("--no-grad-reduce", action="store_true",
+                    help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
 
@@ -367,7 +367,7 @@ def main():
     e2e = run_e2e(opt, model, dev, args, barrier, world)
 
     grad_reduce = None
-    if args.grad_reduce and world > 1:
+    if not args.no_grad_reduce and world > 1:
         del opt
         grad_reduce = run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier)
 

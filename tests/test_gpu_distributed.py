@@ -143,10 +143,10 @@ def test_two_gpu_sharded_step_is_bit_identical():
     assert out == {0: "ok", 1: "ok"}, out
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_two_gpu_fused_gradient_reduction(dtype):
+@pytest.mark.parametrize("world,dtype", [(2, torch.float32), (2, torch.bfloat16), (4, torch.float32)])
+def test_fused_gradient_reduction(world, dtype):
     """Each rank's own gradients, summed over NVLink inside the AdamW and Muon-prep kernels."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    out = _spawn(_worker_reduce, 2, dtype)
-    assert out == {0: "ok", 1: "ok"}, out
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = _spawn(_worker_reduce, world, dtype)
+    assert out == {r: "ok" for r in range(world)}, out
