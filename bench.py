@@ -368,6 +368,7 @@ def main():
 
     grad_reduce = None
     if not args.no_grad_reduce and world > 1:
+        opt.close()
         del opt
         grad_reduce = run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier)
 

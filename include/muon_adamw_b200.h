@@ -223,6 +223,12 @@ int mad_ipc_free(void* dev_ptr);
 int mad_ipc_open(const void* handle, void** peer_ptr);
 int mad_ipc_close(void* peer_ptr);
 
+/* Copies `bytes` from src to dst -- device buffers of this node, local or
+ * mapped with mad_ipc_open -- on `stream`, by the copy engines (one
+ * cudaMemcpyAsync; no SM is used).  The sharded step pushes each rank's
+ * updated parameters into the other ranks' replicas with it. */
+int mad_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* Copies the plan's device status word to *status (synchronises `stream`)
  * and, if clear != 0, resets it.  Non-zero bits mean a kernel gave up
  * waiting on a barrier; the step's results are then invalid. */

@@ -108,6 +108,9 @@ def _worker(rank, world, port, q):
             assert torch.equal(sd["muon"]["state"][i]["momentum_buffer"], ref["muon"]["state"][i]["momentum_buffer"])
         for i in ref["adam"]["state"]:
             assert torch.equal(sd["adam"]["state"][i]["exp_avg_sq"], ref["adam"]["state"][i]["exp_avg_sq"])
+        sharded.close()
+        for p, p1 in zip(adam + muon, adam1 + muon1):     # parameters survive close() as private copies
+            assert torch.equal(p.detach(), p1.detach())
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))

@@ -1,7 +1,9 @@
 // Peer buffers: device memory the other processes of this node map with CUDA
 // IPC, so a kernel on one GPU can read another rank's gradients over NVLink
-// with plain loads (no multicast, no TMA from peer memory).  These are the
-// only entry points of the library that allocate.
+// with plain loads (no multicast, no TMA from peer memory), and the copy
+// engines can write updated parameters straight into the other ranks'
+// replicas.  mad_ipc_alloc is the only entry point of the library that
+// allocates.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -59,4 +61,13 @@ extern "C" int mad_ipc_close(void* peer_ptr) {
   if (!peer_ptr) return MAD_OK;
   const cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
   return e == cudaSuccess ? MAD_OK : cuda_fail(e, "mad_ipc_close");
+}
+
+extern "C" int mad_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  clear_error();
+  if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(MAD_ERR_INVALID, "mad_copy_async: bad arguments");
+  if (bytes == 0) return MAD_OK;
+  const cudaError_t e =
+      cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MAD_OK : cuda_fail(e, "mad_copy_async");
 }

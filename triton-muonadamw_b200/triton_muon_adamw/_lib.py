@@ -92,6 +92,7 @@ SIGNATURES = {
     "mad_ipc_free": (ctypes.c_int, [c_void_p]),
     "mad_ipc_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "mad_ipc_close": (ctypes.c_int, [c_void_p]),
+    "mad_copy_async": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
 }
 
 _lib = None

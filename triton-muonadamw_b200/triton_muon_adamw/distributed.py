@@ -14,10 +14,15 @@ optimizer step needs, with one real exchange step:
   A tensor may straddle two ranges; each rank updates its piece.
 * **Exchange.**  Parameters are re-homed as views into flat buffers laid out
   so that every rank's updated elements form one contiguous segment at
-  offset ``rank * segment``: one in-place ``all_gather_into_tensor`` per
-  buffer refreshes every replica.  The AdamW gather starts right after the
-  AdamW launch and each Muon bucket's gather right after that bucket's
-  launches, so NCCL traffic over NVLink overlaps the remaining work.
+  offset ``rank * segment``.  On GPUs the flats live in a peer arena (CUDA
+  IPC) and each rank pushes its segment into every other rank's replica with
+  the copy engines (``mad_copy_async``, one side stream per peer), right
+  after the AdamW launch and after each Muon bucket's launches: the transfers
+  use no SM, so they overlap the persistent Newton-Schulz GEMMs, which hold
+  every SM.  Stream-ordered barriers (a one-element all-reduce) open and
+  close a step, so no rank writes a replica its owner may still be reading.
+  Without a peer arena (the CPU test backend) one in-place
+  ``all_gather_into_tensor`` per buffer does the same.
 
 Gradients are expected to be identical on every rank already (data-parallel
 all-reduce upstream) -- unless ``reduce_grads`` is set: then each rank's
@@ -42,6 +47,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .adamw.cuda_adam import AdamWTable
 from .muon.cuda_muon import ADJUST_LR_FNS, MuonPlan, lr_scale, run_muon_plan
 
@@ -169,6 +175,40 @@ class CudaBackend:
         from .peer import PeerArena  # noqa: PLC0415
         return PeerArena(nbytes, device, process_group)
 
+    def param_arena(self, nbytes: int, device, process_group):
+        """The parameter flats' arena: every rank writes its updated segments into the others' copies."""
+        from .peer import PeerArena  # noqa: PLC0415
+        return PeerArena(nbytes, device, process_group)
+
+    def push_segment(self, arena, flat: torch.Tensor, seg: int, rank: int):
+        """Copy this rank's segment of ``flat`` into every other rank's replica with the copy engines.
+
+        One ``cudaMemcpyAsync`` per peer, each on its own side stream (so the
+        copies to different peers run concurrently), ordered after the work
+        queued so far on the current stream; rank r serves peers r+1, r+2, ...
+        in turn so that the ranks' copies spread over the switch.  Returns a
+        work whose ``wait()`` makes the current stream wait for all of them.
+        """
+        lib = _lib.load()
+        cur = torch.cuda.current_stream()
+        if not hasattr(self, "_push_streams"):
+            self._push_streams = [torch.cuda.Stream(device=cur.device) for _ in range(arena.world - 1)]
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        src = flat[rank * seg:(rank + 1) * seg]
+        off = src.data_ptr() - arena.ptr
+        nbytes = src.numel() * src.element_size()
+        done = []
+        for k in range(1, arena.world):
+            st = self._push_streams[k - 1]
+            st.wait_event(ready)
+            _lib.check(lib.mad_copy_async(arena.peer_ptrs[(rank + k) % arena.world] + off, src.data_ptr(), nbytes,
+                                          st.cuda_stream), "mad_copy_async")
+            e = torch.cuda.Event()
+            e.record(st)
+            done.append(e)
+        return _StreamWork(done)
+
     def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None, reduce=None):
         if not quads:
             return
@@ -192,6 +232,18 @@ class CudaBackend:
         for plan in self.plans.values():
             st |= plan.read_status()
         return st
+
+
+class _StreamWork:
+    """Completion of copies queued on side streams: ``wait()`` orders the current stream after them."""
+
+    def __init__(self, events):
+        self.events = events
+
+    def wait(self):
+        cur = torch.cuda.current_stream()
+        for e in self.events:
+            cur.wait_event(e)
 
 
 class _Branch:
@@ -240,21 +292,33 @@ class ShardedMuonAdamW:
         mu.a, mu.b, mu.c = muon_config.coeffs
         mu.is_nesterov, mu.steps, mu.adjust_lr_fn = muon_config.nesterov, muon_config.ns_steps, muon_config.adjust_lr_fn
 
-        # AdamW: ZeRO-1 ranges over one flat buffer.
+        # AdamW: ZeRO-1 ranges over one flat buffer.  Muon: owner segments per bucket.
         self.adam_numels = [p.numel() for p in ad.model_params]
         self.adam_offsets, self.adam_shard, total = zero1_layout(self.adam_numels, self.world)
-        self.adam_flat = torch.zeros(total, dtype=self.dtype, device=self.device)
-        _rehome(ad.model_params, self.adam_flat, self.adam_offsets)
         lo = self.rank * self.adam_shard
         self.adam_pieces = shard_pieces(self.adam_offsets, self.adam_numels, lo, lo + self.adam_shard)
         self.exp_avg = torch.zeros(self.adam_shard, dtype=torch.float32, device=self.device)
         self.exp_avg_sq = torch.zeros(self.adam_shard, dtype=torch.float32, device=self.device)
-
-        # Muon: owner segments per bucket.
         shapes = [tuple(p.shape) for p in mu.model_params]
         self.slots, self.seg_sizes = muon_layout(shapes, self.world, n_buckets)
-        self.muon_flats = [torch.zeros(self.world * seg, dtype=self.dtype, device=self.device)
-                           for seg in self.seg_sizes]
+
+        # The flat buffers, in a peer arena when the backend has one (the updated
+        # segments are then pushed into the other ranks' replicas by the copy
+        # engines), else ordinary device memory gathered with NCCL.
+        self.param_arena = None
+        nbytes, adam_bytes, bucket_base = self._flat_layout(total)
+        if hasattr(self.backend, "param_arena"):
+            self.param_arena = self.backend.param_arena(nbytes, self.device, self.pg)
+            raw = self.param_arena.tensor
+            es = self._elem_size()
+            self.adam_flat = raw[0:total * es].view(self.dtype)
+            self.muon_flats = [raw[base:base + self.world * seg * es].view(self.dtype)
+                               for base, seg in zip(bucket_base, self.seg_sizes)]
+        else:
+            self.adam_flat = torch.zeros(total, dtype=self.dtype, device=self.device)
+            self.muon_flats = [torch.zeros(self.world * seg, dtype=self.dtype, device=self.device)
+                               for seg in self.seg_sizes]
+        _rehome(ad.model_params, self.adam_flat, self.adam_offsets)
         with torch.no_grad():
             for p, s in zip(mu.model_params, self.slots):
                 view = self.muon_flats[s.bucket][s.offset:s.offset + s.numel].view_as(p)
@@ -274,17 +338,26 @@ class ShardedMuonAdamW:
         if reduce_grads is not None:
             self._make_grad_arena()
 
-    # ------------------------------------------------------------------ gradient arena
-    def _make_grad_arena(self):
-        """Gradient views laid out like the parameter flats, in one arena every rank maps."""
-        es = torch.empty((), dtype=self.dtype).element_size()
-        ad, mu = self.adamw, self.muon
-        off = _round_up(len(self.adam_flat) * es, 256)
+    # ------------------------------------------------------------------ arenas
+    def _elem_size(self) -> int:
+        return torch.empty((), dtype=self.dtype).element_size()
+
+    def _flat_layout(self, adam_total: int):
+        """Byte layout shared by the parameter and gradient arenas: the AdamW flat, then each bucket's flat."""
+        es = self._elem_size()
+        off = adam_bytes = _round_up(adam_total * es, 256)
         bucket_base = []
         for seg in self.seg_sizes:
             bucket_base.append(off)
             off += _round_up(self.world * seg * es, 256)
-        self.arena = self.backend.grad_arena(off, self.device, self.pg)
+        return off, adam_bytes, bucket_base
+
+    def _make_grad_arena(self):
+        """Gradient views laid out like the parameter flats, in one arena every rank maps."""
+        es = self._elem_size()
+        ad, mu = self.adamw, self.muon
+        nbytes, _, bucket_base = self._flat_layout(len(self.adam_flat))
+        self.arena = self.backend.grad_arena(nbytes, self.device, self.pg)
         raw = self.arena.tensor
 
         def view(byte_off, p):
@@ -314,13 +387,22 @@ class ShardedMuonAdamW:
         dist.all_reduce(self._sync_flag, group=self.pg)
 
     def close(self):
-        """Release the gradient arena (collective; with ``reduce_grads``).  Gradients are set to None."""
+        """Release the memory shared with the other ranks (collective).  The parameters move to private
+        copies; gradients in the shared gradient buffer are dropped (set to None).  No step afterwards."""
         if self.arena is not None:
             for p, _ in self._grad_views:
                 p.grad = None
             self._grad_views = []
             self.arena.close()
             self.arena = None
+        if self.param_arena is not None:
+            with torch.no_grad():
+                for p in list(self.adamw.model_params) + list(self.muon.model_params):
+                    p.data = p.data.clone()
+            self.adam_flat, self.muon_flats = None, []
+            self.param_arena.close()
+            self.param_arena = None
+            self.closed = True
 
     # ------------------------------------------------------------------ step
     def _adam_quads(self):
@@ -344,6 +426,9 @@ class ShardedMuonAdamW:
         return out
 
     def _gather(self, flat: torch.Tensor, seg: int):
+        """Refresh every replica of ``flat`` with this rank's segment (returns a work with ``wait()``)."""
+        if self.param_arena is not None:
+            return self.backend.push_segment(self.param_arena, flat, seg, self.rank)
         mine = flat[self.rank * seg:(self.rank + 1) * seg]
         return dist.all_gather_into_tensor(flat, mine, group=self.pg, async_op=True)
 
@@ -356,12 +441,17 @@ class ShardedMuonAdamW:
         works = []
         bias1, bias2 = 1 - ad.beta1 ** ad.step_num, 1 - ad.beta2 ** ad.step_num
         red = None
+        if getattr(self, "closed", False):
+            raise RuntimeError("this optimizer was closed (close()); it cannot step")
         if self.reduce_grads is not None:
             if self.arena is None:
                 raise RuntimeError("the gradient arena was released (close()); this optimizer cannot step")
             self._bind_grads()
             red = self.arena.spec(1.0 / self.world if self.reduce_grads == "mean" else 1.0)
-            self._rank_sync()      # every rank's gradients are complete before any rank reads them
+        if red is not None or self.param_arena is not None:
+            # Every rank's gradients are complete before any rank reads them, and no rank writes
+            # into another's parameter replica while that rank's forward/backward may still read it.
+            self._rank_sync()
         if wait_for:
             wait_for[0]()
         if self.adam_shard:
@@ -378,8 +468,10 @@ class ShardedMuonAdamW:
                 works.append(self._gather(self.muon_flats[b], seg))
         for w in works:
             w.wait()
-        if red is not None:
-            self._rank_sync()      # no rank overwrites its gradients while another may still read them
+        if red is not None or self.param_arena is not None:
+            # No rank overwrites its gradients while another may still read them, and every
+            # rank's pushes into this rank's replicas have landed before step() returns.
+            self._rank_sync()
 
     @torch.no_grad()
     def step_from_host(self, host_grads):
