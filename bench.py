@@ -239,6 +239,8 @@ def main():
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--push", default=None, choices=["kernel", "copy_engine"],
+                    help="at N>1, how updated parameters reach the other ranks (default: the library's choice)")
     ap.add_argument("--no-grad-reduce", action="store_true",
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
     args = ap.parse_args()
@@ -278,6 +280,9 @@ def main():
                       ns_steps=args.ns_steps)
     acfg = AdamConfig(**cfg["adam"])
     opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg)
+    if args.push and opt.distributed is not None:
+        opt.distributed.backend.push = args.push
+    push_mode = opt.distributed.backend.push if opt.distributed is not None else None
     n_muon, n_adam = len(opt.muon.model_params), len(opt.adamw.model_params)
 
     def barrier():
@@ -387,6 +392,7 @@ def main():
             "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "muon_matrices": n_muon,
                        "adamw_tensors": n_adam, "ns_steps": args.ns_steps, "coeffs": list(COEFFS),
                        "parallelism": "single-gpu" if world == 1 else f"muon-owner+zero1-adamw x{world}",
+                       "param_push": push_mode,
                        "l2": "inputs (fp32 grads/params/momentum, > 100 GB) exceed L2; no flush needed",
                        "elementwise_dtype": "fp32"},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": int(round(launches_per_step * args.steps)),

@@ -229,6 +229,21 @@ int mad_ipc_close(void* peer_ptr);
  * updated parameters into the other ranks' replicas with it. */
 int mad_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
 
+/* Other ranks' copies of a buffer: rank k's copy of the byte at address a is
+ * at a + delta[k] (mapped with mad_ipc_open). */
+typedef struct mad_peer_set {
+  int32_t n_peers; /* 0..MAD_MAX_RANKS */
+  int32_t pad;
+  int64_t delta[MAD_MAX_RANKS];
+} mad_peer_set;
+
+/* Writes the `bytes` at src (16-byte aligned, a multiple of 16) into every
+ * peer's copy with one small kernel on `stream`: each 16-byte vector is read
+ * once and stored to all peers over NVLink.  Its CTAs (128 threads, no shared
+ * memory) fit beside the persistent GEMM's, so the broadcast runs during the
+ * Newton-Schulz work: the all-gather of the sharded step. */
+int mad_peer_push(const void* src, int64_t bytes, const mad_peer_set* peers, void* stream);
+
 /* Copies the plan's device status word to *status (synchronises `stream`)
  * and, if clear != 0, resets it.  Non-zero bits mean a kernel gave up
  * waiting on a barrier; the step's results are then invalid. */

@@ -32,9 +32,9 @@ ADAM = dict(lr=3e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
 class CpuArena:
     """The gradient arena of CPU ranks: a plain tensor; a reduction all-gathers every rank's arena."""
 
-    def __init__(self, nbytes, device, pg):
+    def __init__(self, nbytes, device, process_group):
         self.tensor = torch.zeros(nbytes, dtype=torch.uint8)
-        self.pg = pg
+        self.pg = process_group
 
     def spec(self, scale):
         return (self, scale)
@@ -57,8 +57,8 @@ def reduced(g, copies, arena, scale):
 class OracleBackend:
     """CPU arithmetic for the sharded step (test only)."""
 
-    def grad_arena(self, nbytes, device, pg):
-        return CpuArena(nbytes, device, pg)
+    def grad_arena(self, nbytes, device, process_group):
+        return CpuArena(nbytes, device, process_group)
 
     @staticmethod
     def _gather(reduce):
@@ -250,3 +250,19 @@ def test_rank_that_leaves_surfaces_as_collective_error():
     out = _run(2, "die")
     assert out.get(1) == "left"
     assert out.get(0, "").split(":")[0] in ("RuntimeError", "DistBackendError", "DistError"), out
+
+
+def test_cuda_backend_offers_every_call_the_sharded_step_makes():
+    """The CPU runs above use OracleBackend; the CUDA backend must take the same calls."""
+    import inspect
+
+    from triton_muon_adamw.distributed import CudaBackend
+    def params(fn):
+        return [(p.name, p.kind, p.default) for p in inspect.signature(fn).parameters.values()]
+
+    for name in ("adamw", "muon", "grad_arena"):
+        assert params(getattr(CudaBackend, name)) == params(getattr(OracleBackend, name)), name
+    for name in ("status", "param_arena", "push_segment"):
+        assert callable(getattr(CudaBackend, name, None)), name
+    with pytest.raises(ValueError):
+        CudaBackend(push="nccl")

@@ -71,3 +71,67 @@ extern "C" int mad_copy_async(void* dst, const void* src, int64_t bytes, void* s
       cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MAD_OK : cuda_fail(e, "mad_copy_async");
 }
+
+namespace {
+
+constexpr int PUSH_THREADS = 128;
+constexpr int PUSH_UNROLL = 4;
+
+struct PeerSet {
+  int32_t n;
+  int64_t delta[MAX_RANKS];
+};
+
+// Each thread loads PUSH_UNROLL 16-byte vectors of the source once and stores
+// them to every peer's copy (rank-rotated start per CTA, so the ranks' CTAs
+// spread over the switch).  128 threads, <= 64 registers, no shared memory:
+// one CTA fits on an SM beside the persistent Newton-Schulz GEMM CTA (which
+// leaves 11,776 registers and 1 KB of shared memory free), so the broadcast
+// overlaps the GEMMs instead of waiting for them.
+__global__ void __launch_bounds__(PUSH_THREADS, 1) peer_push_kernel(const uint4* __restrict__ src, int64_t n_vec,
+                                                                    PeerSet ps) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * PUSH_THREADS;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * PUSH_THREADS + threadIdx.x; base < n_vec;
+       base += stride * PUSH_UNROLL) {
+    uint4 v[PUSH_UNROLL];
+#pragma unroll
+    for (int u = 0; u < PUSH_UNROLL; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < n_vec) v[u] = __ldcs(src + i);
+    }
+    for (int j = 0; j < ps.n; ++j) {
+      const int k = (j + blockIdx.x) % ps.n;
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(const_cast<uint4*>(src)) + ps.delta[k]);
+#pragma unroll
+      for (int u = 0; u < PUSH_UNROLL; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < n_vec) dst[i] = v[u];
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+}  // namespace
+
+extern "C" int mad_peer_push(const void* src, int64_t bytes, const mad_peer_set* peers, void* stream) {
+  clear_error();
+  if (bytes < 0 || !peers || (bytes > 0 && !src)) return fail(MAD_ERR_INVALID, "mad_peer_push: bad arguments");
+  if (peers->n_peers < 0 || peers->n_peers > MAX_RANKS)
+    return fail(MAD_ERR_INVALID, "mad_peer_push: n_peers %d outside 0..%d", peers->n_peers, MAX_RANKS);
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0 || (bytes & 15) != 0)
+    return fail(MAD_ERR_ALIGN, "mad_peer_push: source and size must be multiples of 16 bytes");
+  for (int k = 0; k < peers->n_peers; ++k)
+    if ((peers->delta[k] & 15) != 0) return fail(MAD_ERR_ALIGN, "mad_peer_push: peer %d is not 16-byte aligned", k);
+  if (bytes == 0 || peers->n_peers == 0) return MAD_OK;
+  PeerSet ps;
+  std::memset(&ps, 0, sizeof(ps));
+  ps.n = peers->n_peers;
+  for (int k = 0; k < ps.n; ++k) ps.delta[k] = peers->delta[k];
+  const int64_t n_vec = bytes / 16;
+  const int64_t want = (n_vec + PUSH_THREADS * PUSH_UNROLL - 1) / (PUSH_THREADS * PUSH_UNROLL);
+  const int grid = static_cast<int>(want < num_sms() ? want : num_sms());
+  peer_push_kernel<<<grid, PUSH_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint4*>(src),
+                                                                                n_vec, ps);
+  return check_launch("peer_push_kernel");
+}

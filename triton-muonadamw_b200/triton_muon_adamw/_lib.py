@@ -53,6 +53,10 @@ class GradReduce(ctypes.Structure):
     _fields_ = [("n_ranks", c_int32), ("scale", c_float), ("delta", c_int64 * MAX_RANKS)]
 
 
+class PeerSet(ctypes.Structure):
+    _fields_ = [("n_peers", c_int32), ("pad", c_int32), ("delta", c_int64 * MAX_RANKS)]
+
+
 # name -> (restype, argtypes); every entry point declared in include/muon_adamw_b200.h
 SIGNATURES = {
     "mad_last_error": (ctypes.c_char_p, []),
@@ -93,6 +97,7 @@ SIGNATURES = {
     "mad_ipc_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "mad_ipc_close": (ctypes.c_int, [c_void_p]),
     "mad_copy_async": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "mad_peer_push": (ctypes.c_int, [c_void_p, c_int64, ctypes.POINTER(PeerSet), c_void_p]),
 }
 
 _lib = None

@@ -15,12 +15,14 @@ optimizer step needs, with one real exchange step:
 * **Exchange.**  Parameters are re-homed as views into flat buffers laid out
   so that every rank's updated elements form one contiguous segment at
   offset ``rank * segment``.  On GPUs the flats live in a peer arena (CUDA
-  IPC) and each rank pushes its segment into every other rank's replica with
-  the copy engines (``mad_copy_async``, one side stream per peer), right
-  after the AdamW launch and after each Muon bucket's launches: the transfers
-  use no SM, so they overlap the persistent Newton-Schulz GEMMs, which hold
-  every SM.  Stream-ordered barriers (a one-element all-reduce) open and
-  close a step, so no rank writes a replica its owner may still be reading.
+  IPC) and each rank pushes its segment into every other rank's replica
+  right after the AdamW launch and after each Muon bucket's launches, on a
+  side stream, with a small broadcast kernel (``mad_peer_push``) whose CTAs
+  fit beside the persistent Newton-Schulz GEMM's -- so the transfer runs
+  during the GEMMs, where NCCL's kernels would wait for free SMs -- or with
+  the copy engines (``CudaBackend(push="copy_engine")``).  Stream-ordered
+  barriers (a one-element all-reduce) open and close a step, so no rank
+  writes a replica its owner may still be reading.
   Without a peer arena (the CPU test backend) one in-place
   ``all_gather_into_tensor`` per buffer does the same.
 
@@ -41,6 +43,7 @@ inject a CPU checker backend instead; the optimizer itself never selects one.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -164,9 +167,12 @@ def _rehome(params, flat: torch.Tensor, offsets) -> None:
 
 # --------------------------------------------------------------------------- backends
 class CudaBackend:
-    """The product's arithmetic: the CUDA AdamW and Muon kernels."""
+    """The product's arithmetic: the CUDA AdamW and Muon kernels, and the peer transfers."""
 
-    def __init__(self):
+    def __init__(self, push: str = "kernel"):
+        if push not in ("kernel", "copy_engine"):
+            raise ValueError(f"push must be 'kernel' or 'copy_engine', got {push!r}")
+        self.push = push
         self.adam_table = AdamWTable()
         self.plans = {}
 
@@ -181,33 +187,48 @@ class CudaBackend:
         return PeerArena(nbytes, device, process_group)
 
     def push_segment(self, arena, flat: torch.Tensor, seg: int, rank: int):
-        """Copy this rank's segment of ``flat`` into every other rank's replica with the copy engines.
+        """Write this rank's segment of ``flat`` into every other rank's replica, after the work queued so
+        far on the current stream; returns a work whose ``wait()`` orders the current stream after it.
 
-        One ``cudaMemcpyAsync`` per peer, each on its own side stream (so the
-        copies to different peers run concurrently), ordered after the work
-        queued so far on the current stream; rank r serves peers r+1, r+2, ...
-        in turn so that the ranks' copies spread over the switch.  Returns a
-        work whose ``wait()`` makes the current stream wait for all of them.
+        ``push="kernel"`` (default): one ``mad_peer_push`` launch on a side stream -- a
+        small kernel whose CTAs fit beside the persistent GEMM's, reading each
+        vector once and storing it to every peer over NVLink.  ``push="copy_engine"``:
+        one ``cudaMemcpyAsync`` per peer, each on its own side stream (no SM
+        at all, but the copy engines reach about half the NVLink rate).
         """
         lib = _lib.load()
         cur = torch.cuda.current_stream()
-        if not hasattr(self, "_push_streams"):
-            self._push_streams = [torch.cuda.Stream(device=cur.device) for _ in range(arena.world - 1)]
+        n_streams = 1 if self.push == "kernel" else arena.world - 1
+        if len(getattr(self, "_push_streams", ())) != n_streams:
+            self._push_streams = [torch.cuda.Stream(device=cur.device) for _ in range(n_streams)]
         ready = torch.cuda.Event()
         ready.record(cur)
         src = flat[rank * seg:(rank + 1) * seg]
         off = src.data_ptr() - arena.ptr
         nbytes = src.numel() * src.element_size()
+        peers = [(rank + k) % arena.world for k in range(1, arena.world)]
         done = []
-        for k in range(1, arena.world):
-            st = self._push_streams[k - 1]
+        if self.push == "kernel":
+            st = self._push_streams[0]
             st.wait_event(ready)
-            _lib.check(lib.mad_copy_async(arena.peer_ptrs[(rank + k) % arena.world] + off, src.data_ptr(), nbytes,
-                                          st.cuda_stream), "mad_copy_async")
+            ps = _lib.PeerSet()
+            ps.n_peers = len(peers)
+            for j, q in enumerate(peers):
+                ps.delta[j] = arena.peer_ptrs[q] - arena.ptr
+            _lib.check(lib.mad_peer_push(src.data_ptr(), nbytes, ctypes.byref(ps), st.cuda_stream), "mad_peer_push")
             e = torch.cuda.Event()
             e.record(st)
             done.append(e)
+        else:
+            for st, q in zip(self._push_streams, peers):
+                st.wait_event(ready)
+                _lib.check(lib.mad_copy_async(arena.peer_ptrs[q] + off, src.data_ptr(), nbytes, st.cuda_stream),
+                           "mad_copy_async")
+                e = torch.cuda.Event()
+                e.record(st)
+                done.append(e)
         return _StreamWork(done)
+
 
     def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None, reduce=None):
         if not quads:
