@@ -78,16 +78,19 @@ def lpt_assign(costs, n_ranks: int) -> list[int]:
     return owner
 
 
-def split_buckets(costs, n_buckets: int) -> list[int]:
+def split_buckets(costs, n_buckets: int, increasing: bool = False) -> list[int]:
     """Contiguous groups in parameter order with decreasing total cost (weights n, n-1, ..., 1).
 
     Each bucket's all-gather overlaps the compute of the buckets after it; only
     the last one's is exposed, so the last bucket is made the smallest while
     every earlier gather still fits under the (larger) compute that follows it.
+    ``increasing=True`` gives weights 1, 2, ..., n instead: for a pipeline whose
+    first stage is a copy (gradients from the host), a small first bucket
+    starts the compute early.
     """
     n_buckets = max(1, min(n_buckets, len(costs)))
     total = sum(costs) or 1.0
-    weights = [n_buckets - k for k in range(n_buckets)]
+    weights = [k + 1 if increasing else n_buckets - k for k in range(n_buckets)]
     bounds, acc = [], 0.0
     for w in weights:
         acc += w

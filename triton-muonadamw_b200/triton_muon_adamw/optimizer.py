@@ -203,16 +203,20 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         self.muon.step()
 
     @torch.no_grad()
-    def step_from_host(self, host_grads, n_buckets: int = 5) -> None:
+    def step_from_host(self, host_grads, n_buckets: int = 8) -> None:
         """One step whose gradients live in (pinned) host memory.
 
         ``host_grads`` maps each parameter to its host gradient (a dict keyed by
         Parameter, or a sequence in the order ``param_group["adam"] +
         param_group["muon"]``).  The result equals copying every gradient into
         ``param.grad`` and calling :meth:`step`, but the host-to-device copies
-        run on a side stream in the order the work consumes them -- AdamW
-        first, then the Muon matrices in buckets of decreasing size -- so each
-        bucket's Newton-Schulz work overlaps the copies of the next.
+        run on a side stream while the GPU computes: a two-stage pipeline
+        (copy, then compute) ordered by Johnson's rule -- the Muon matrices,
+        whose compute outweighs their copy, first, in buckets of increasing
+        size so the compute starts after a short copy; the AdamW tensors,
+        whose copy outweighs their compute, last, their copy hidden under the
+        Muon work.  The two branches update disjoint parameters, so the order
+        does not change any result.
         """
         params = list(self.param_group["adam"]) + list(self.param_group["muon"])
         if not isinstance(host_grads, dict):
@@ -243,13 +247,12 @@ class MuonAdamW(TritonMuon, TritonAdamW):
             ev.record(copy)
             return ev
 
-        main.wait_event(upload(self.adamw.model_params))
-        self.adamw.step()
         mu = self.muon
         mats = [p for p in mu.model_params if p in host_grads or p.grad is not None]
-        buckets = split_buckets([ns_cost(p.shape) for p in mats], n_buckets) if mats else []
+        buckets = split_buckets([ns_cost(p.shape) for p in mats], n_buckets, increasing=True) if mats else []
         groups = [[p for p, b in zip(mats, buckets) if b == k] for k in range(max(buckets) + 1 if buckets else 0)]
         events = [upload(g) for g in groups]
+        adam_ready = upload(self.adamw.model_params)
         for k, (g, ev) in enumerate(zip(groups, events)):
             main.wait_event(ev)
             triples = mu._active(only=g)
@@ -259,6 +262,8 @@ class MuonAdamW(TritonMuon, TritonAdamW):
             plan.ensure(triples, mu.adjust_lr_fn, triples[0][0].device)
             run_muon_plan(plan, beta=mu.beta, nesterov=mu.is_nesterov, a=mu.a, b=mu.b, c=mu.c, ns_steps=mu.steps,
                           eps=mu.eps, lr=mu.lr, weight_decay=mu.weight_decay)
+        main.wait_event(adam_ready)
+        self.adamw.step()
         for p in params:
             if p.grad is not None:
                 p.grad.record_stream(copy)
