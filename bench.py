@@ -239,8 +239,8 @@ def main():
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--push", default=None, choices=["kernel", "copy_engine"],
-                    help="at N>1, how updated parameters reach the other ranks (default: the library's choice)")
+    ap.add_argument("--push", default="auto", choices=["auto", "nccl", "copy_engine", "kernel", "hybrid"],
+                    help="at N>1, how updated parameters reach the other ranks (MuonAdamW peer_push)")
     ap.add_argument("--no-grad-reduce", action="store_true",
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
     args = ap.parse_args()
@@ -279,10 +279,9 @@ def main():
     mcfg = MuonConfig(lr=1e-3, beta=0.95, eps=1e-7, weight_decay=0.1, coeffs=COEFFS, nesterov=True,
                       ns_steps=args.ns_steps)
     acfg = AdamConfig(**cfg["adam"])
-    opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg)
-    if args.push and opt.distributed is not None:
-        opt.distributed.backend.push = args.push
-    push_mode = opt.distributed.backend.push if opt.distributed is not None else None
+    opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg,
+                    peer_push=args.push)
+    push_mode = opt.distributed.backend.push if opt.distributed is not None else None   # "auto" resolved
     n_muon, n_adam = len(opt.muon.model_params), len(opt.adamw.model_params)
 
     def barrier():
@@ -487,7 +486,7 @@ def run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier):
     gc.collect()
     torch.cuda.empty_cache()
     opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg,
-                    reduce_grads="mean")
+                    reduce_grads="mean", peer_push=args.push)
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     for p in model.parameters():
         p.grad.normal_(0.0, 1e-3, generator=gen)

@@ -265,4 +265,4 @@ def test_cuda_backend_offers_every_call_the_sharded_step_makes():
     for name in ("status", "param_arena", "push_segment"):
         assert callable(getattr(CudaBackend, name, None)), name
     with pytest.raises(ValueError):
-        CudaBackend(push="nccl")
+        CudaBackend(push="tree")

@@ -172,10 +172,14 @@ def _rehome(params, flat: torch.Tensor, offsets) -> None:
 class CudaBackend:
     """The product's arithmetic: the CUDA AdamW and Muon kernels, and the peer transfers."""
 
-    def __init__(self, push: str = "kernel"):
-        if push not in ("kernel", "copy_engine"):
-            raise ValueError(f"push must be 'kernel' or 'copy_engine', got {push!r}")
+    PUSH_MODES = ("auto", "nccl", "copy_engine", "kernel", "hybrid")
+
+    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5):
+        if push not in self.PUSH_MODES:
+            raise ValueError(f"push must be one of {self.PUSH_MODES}, got {push!r}")
         self.push = push
+        self.ce_splits = max(1, int(ce_splits))
+        self.ce_fraction = float(ce_fraction)
         self.adam_table = AdamWTable()
         self.plans = {}
 
@@ -185,7 +189,19 @@ class CudaBackend:
         return PeerArena(nbytes, device, process_group)
 
     def param_arena(self, nbytes: int, device, process_group):
-        """The parameter flats' arena: every rank writes its updated segments into the others' copies."""
+        """The parameter flats' arena: every rank writes its updated segments into the others' copies.
+
+        None for ``push="nccl"`` (plain device memory, NCCL all-gathers).  ``"auto"``
+        picks by group size, from 8B-step measurements: the copy engines up to
+        4 ranks (they carry the (N-1)/N x parameter bytes each rank sends under
+        the GEMMs, using no SM), NCCL beyond (its NVLS all-gather sends each
+        segment once and the switch replicates it, where the copy engines'
+        ~310 GB/s of peer writes no longer hide under the compute).
+        """
+        if self.push == "auto":
+            self.push = "copy_engine" if dist.get_world_size(process_group) <= 4 else "nccl"
+        if self.push == "nccl":
+            return None
         from .peer import PeerArena  # noqa: PLC0415
         return PeerArena(nbytes, device, process_group)
 
@@ -193,45 +209,57 @@ class CudaBackend:
         """Write this rank's segment of ``flat`` into every other rank's replica, after the work queued so
         far on the current stream; returns a work whose ``wait()`` orders the current stream after it.
 
-        ``push="kernel"`` (default): one ``mad_peer_push`` launch on a side stream -- a
+        ``push="kernel"``: one ``mad_peer_push`` launch on a side stream -- a
         small kernel whose CTAs fit beside the persistent GEMM's, reading each
-        vector once and storing it to every peer over NVLink.  ``push="copy_engine"``:
-        one ``cudaMemcpyAsync`` per peer, each on its own side stream (no SM
-        at all, but the copy engines reach about half the NVLink rate).
+        vector once and storing it to every peer over NVLink.
+        ``push="copy_engine"``: ``cudaMemcpyAsync`` per peer, each peer's copy cut
+        into ``ce_splits`` pieces on their own streams (no SM at all).
+        ``push="hybrid"``: the first ``ce_fraction`` of the segment by the copy
+        engines, the rest by the kernel, concurrently.
         """
+        if self.push not in ("kernel", "copy_engine", "hybrid"):
+            raise ValueError(f"push mode {self.push!r} does not write into peer replicas")
         lib = _lib.load()
         cur = torch.cuda.current_stream()
-        n_streams = 1 if self.push == "kernel" else arena.world - 1
-        if len(getattr(self, "_push_streams", ())) != n_streams:
-            self._push_streams = [torch.cuda.Stream(device=cur.device) for _ in range(n_streams)]
+        n_peers = arena.world - 1
+        ce_streams = 0 if self.push == "kernel" else n_peers * self.ce_splits
+        while len(getattr(self, "_push_streams", ())) < ce_streams + 1:
+            self._push_streams = getattr(self, "_push_streams", []) + [torch.cuda.Stream(device=cur.device)]
         ready = torch.cuda.Event()
         ready.record(cur)
         src = flat[rank * seg:(rank + 1) * seg]
         off = src.data_ptr() - arena.ptr
         nbytes = src.numel() * src.element_size()
         peers = [(rank + k) % arena.world for k in range(1, arena.world)]
+        ce_bytes = {"kernel": 0, "copy_engine": nbytes}.get(self.push, int(nbytes * self.ce_fraction) // 256 * 256)
         done = []
-        if self.push == "kernel":
+
+        def finish(st):
+            e = torch.cuda.Event()
+            e.record(st)
+            done.append(e)
+
+        if ce_bytes:
+            piece = (-(-ce_bytes // self.ce_splits) + 255) // 256 * 256   # ceil(ce_bytes / splits), 256-aligned
+            streams = iter(self._push_streams[1:])
+            for q in peers:
+                for a in range(0, ce_bytes, piece):
+                    st = next(streams)
+                    st.wait_event(ready)
+                    _lib.check(lib.mad_copy_async(arena.peer_ptrs[q] + off + a, src.data_ptr() + a,
+                                                  min(piece, ce_bytes - a), st.cuda_stream), "mad_copy_async")
+                    finish(st)
+        if ce_bytes < nbytes:
             st = self._push_streams[0]
             st.wait_event(ready)
             ps = _lib.PeerSet()
             ps.n_peers = len(peers)
             for j, q in enumerate(peers):
                 ps.delta[j] = arena.peer_ptrs[q] - arena.ptr
-            _lib.check(lib.mad_peer_push(src.data_ptr(), nbytes, ctypes.byref(ps), st.cuda_stream), "mad_peer_push")
-            e = torch.cuda.Event()
-            e.record(st)
-            done.append(e)
-        else:
-            for st, q in zip(self._push_streams, peers):
-                st.wait_event(ready)
-                _lib.check(lib.mad_copy_async(arena.peer_ptrs[q] + off, src.data_ptr(), nbytes, st.cuda_stream),
-                           "mad_copy_async")
-                e = torch.cuda.Event()
-                e.record(st)
-                done.append(e)
+            _lib.check(lib.mad_peer_push(src.data_ptr() + ce_bytes, nbytes - ce_bytes, ctypes.byref(ps),
+                                         st.cuda_stream), "mad_peer_push")
+            finish(st)
         return _StreamWork(done)
-
 
     def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None, reduce=None):
         if not quads:
@@ -333,6 +361,7 @@ class ShardedMuonAdamW:
         nbytes, adam_bytes, bucket_base = self._flat_layout(total)
         if hasattr(self.backend, "param_arena"):
             self.param_arena = self.backend.param_arena(nbytes, self.device, self.pg)
+        if self.param_arena is not None:
             raw = self.param_arena.tensor
             es = self._elem_size()
             self.adam_flat = raw[0:total * es].view(self.dtype)

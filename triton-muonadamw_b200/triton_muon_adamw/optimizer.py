@@ -155,6 +155,13 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         (:meth:`zero_grad`) to keep them in that buffer; gradients found
         elsewhere at ``step()`` are copied in.  Call :meth:`close` on every
         rank before the process group is destroyed.
+    peer_push:
+        With more than one rank, how each rank's updated parameters reach the
+        others: ``"auto"`` (default; the copy engines up to 4 ranks, NCCL
+        above), ``"nccl"`` (all-gather), ``"copy_engine"`` (each rank writes its
+        segment into the others' replicas with ``cudaMemcpyAsync``, no SM),
+        ``"kernel"`` (a small broadcast kernel beside the GEMMs) or
+        ``"hybrid"`` (copy engines and kernel, half each).
     """
 
     def __init__(
@@ -165,6 +172,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         parameter_split: Literal["auto", "explicit"] = "auto",
         process_group=None,
         reduce_grads: Literal["mean", "sum"] | None = None,
+        peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid"] = "auto",
     ) -> None:
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
@@ -172,9 +180,9 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         self.process_group = process_group
         self.distributed = None
         if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
-            from .distributed import ShardedMuonAdamW  # noqa: PLC0415
+            from .distributed import CudaBackend, ShardedMuonAdamW  # noqa: PLC0415
             self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group,
-                                                reduce_grads=reduce_grads)
+                                                reduce_grads=reduce_grads, backend=CudaBackend(push=peer_push))
             self.adamw = self.distributed.adamw
             self.muon = self.distributed.muon
         else:
