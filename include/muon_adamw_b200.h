@@ -43,15 +43,21 @@ enum {
   MAD_ERR_DEVICE = 5       /* a kernel reported an error in its status word */
 };
 
-/* Element type of parameters, gradients and Muon momentum (the AdamW moments
- * are always float32, as in the reference, triton_adam.py:128-130). */
-enum { MAD_DTYPE_F32 = 0, MAD_DTYPE_BF16 = 1 };
+/* Element types of parameters, gradients and Muon momentum (the AdamW moments
+ * are always float32, as in the reference, triton_adam.py:128-130):
+ *   MAD_DTYPE_F32         param, grad, momentum float32
+ *   MAD_DTYPE_BF16        param, grad, momentum bf16
+ *   MAD_DTYPE_F32_MASTER  param float32 (a master copy), momentum float32, grad
+ *                         bf16; the updated value is also stored, rounded to
+ *                         bf16, to `shadow` (the model's bf16 parameter, same
+ *                         layout as param) -- mixed-precision training. */
+enum { MAD_DTYPE_F32 = 0, MAD_DTYPE_BF16 = 1, MAD_DTYPE_F32_MASTER = 2 };
 
 /* Message describing the last failure on the calling thread ("" if none). */
 const char* mad_last_error(void);
 
 /* ABI version of this library (2: dtype fields in mad_adamw_tensor and mad_muon_matrix;
- * 3: gradient reduction over ranks, CUDA IPC buffers). */
+ * 3: gradient reduction over ranks, CUDA IPC buffers; 4: shadow pointers, F32_MASTER). */
 int32_t mad_abi_version(void);
 
 /* Data-parallel gradients summed over the ranks of one node (no counterpart in
@@ -71,15 +77,17 @@ typedef struct mad_grad_reduce {
 /* ------------------------------------------------------------------ AdamW */
 
 /* One tensor of the AdamW branch (flattened; any shape).  param and grad have
- * type `dtype`; exp_avg and exp_avg_sq are float32.  bf16 parameters are
- * updated in float32 and rounded once on the store. */
+ * the types `dtype` gives; exp_avg and exp_avg_sq are float32.  bf16
+ * parameters are updated in float32 and rounded once on the store. */
 typedef struct mad_adamw_tensor {
-  void* param;       /* element type: dtype */
-  const void* grad;  /* element type: dtype */
+  void* param;       /* element type: float32, or bf16 for MAD_DTYPE_BF16 */
+  const void* grad;  /* element type: float32 for MAD_DTYPE_F32, else bf16 */
   float* exp_avg;
   float* exp_avg_sq;
   int64_t numel;
-  int32_t dtype; /* MAD_DTYPE_F32 or MAD_DTYPE_BF16 */
+  int32_t dtype;     /* MAD_DTYPE_* */
+  int32_t pad;
+  void* shadow;      /* MAD_DTYPE_F32_MASTER: bf16 copy of the updated param; else unused */
 } mad_adamw_tensor;
 
 /* One AdamW update of one float32 tensor, in place (replaces solve_adamw_step,
@@ -110,17 +118,19 @@ int mad_adamw_step_multi_reduce(const void* dev_table, int64_t n_tiles, float lr
 /* ------------------------------------------------------------------ Muon */
 
 /* One Muon matrix (rows x cols, row-major, contiguous); param, grad and
- * momentum all of type `dtype`.  With bf16 the momentum/Nesterov glue and the
- * parameter update round to bf16 after every operation, as the reference's
- * eager ops on bf16 tensors do (triton_muon.py:346-349, 370-372). */
+ * momentum have the types `dtype` gives.  With bf16 the momentum/Nesterov glue
+ * and the parameter update round to bf16 after every operation, as the
+ * reference's eager ops on bf16 tensors do (triton_muon.py:346-349, 370-372). */
 typedef struct mad_muon_matrix {
-  void* param;       /* element type: dtype (also grad and momentum) */
-  const void* grad;
-  void* momentum;
+  void* param;       /* float32, or bf16 for MAD_DTYPE_BF16 */
+  const void* grad;  /* float32 for MAD_DTYPE_F32, else bf16 */
+  void* momentum;    /* the param's type */
   int64_t rows;
   int64_t cols;
   double lr_scale; /* shape adjustment: scaled_lr = float(lr * lr_scale) (triton_muon.py:424-431) */
-  int32_t dtype;   /* MAD_DTYPE_F32 or MAD_DTYPE_BF16 */
+  int32_t dtype;   /* MAD_DTYPE_* */
+  int32_t pad;
+  void* shadow;    /* MAD_DTYPE_F32_MASTER: bf16 copy of the updated param (rows x cols); else unused */
 } mad_muon_matrix;
 
 /* Sizes and launch counts of a Muon plan; filled by mad_muon_plan_size and

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in {HEADER.name} but not exported"
     assert set(declared) == set(_lib.SIGNATURES), "ctypes signatures must cover exactly the header"
-    assert lib.mad_abi_version() == 3
+    assert lib.mad_abi_version() == 4
 
 
 def test_invalid_arguments_fail_before_any_cuda_call():
@@ -173,3 +173,25 @@ def test_state_dict_layout_matches_torch_wrapper():
         for key in ("lr", "weight_decay"):
             assert og[key] == rg[key]
     assert set(ours["muon"]["state"][0]) == {"momentum_buffer"}
+
+
+def test_table_layout_constants_match_the_device_structs():
+    """Tests that read the device plan table directly use these sizes; plan.cuh pins them with static_asserts."""
+    import re
+    from pathlib import Path
+
+    from test_gpu_parity import INV_NORM_OFFSET, MATDESC_BYTES
+    src = (Path(__file__).resolve().parent.parent / "triton-muonadamw_b200" / "csrc" / "plan.cuh").read_text()
+    assert re.search(r"sizeof\(MatDesc\) == (\d+)", src).group(1) == str(MATDESC_BYTES)
+    body = src[src.index("struct MatDesc {"):src.index("float inv_norm;")]
+    off = 0
+    for line in body.splitlines()[1:]:
+        decl = line.split("//")[0].strip().rstrip(";")
+        if not decl:
+            continue
+        names = [n.strip() for n in decl.split(None, 1)[1].split(",")] if "*" not in decl else [decl.split("*")[1]]
+        size = 8 if ("*" in decl or decl.startswith(("double", "int64_t"))) else 4
+        for n in names:
+            m = re.search(r"\[(\d+)\]", n)
+            off += size * (int(m.group(1)) if m else 1)
+    assert off == INV_NORM_OFFSET

@@ -69,20 +69,30 @@ class OracleBackend:
 
     def adamw(self, quads, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, timer=None, reduce=None):
         copies = self._gather(reduce) if reduce is not None else None
-        for p, g, m, v in quads:
+        for q in quads:
+            (p, g, m, v), shadow = q[:4], (q[4] if len(q) > 4 else None)
             if reduce is not None:
                 g = reduced(g, copies, *reduce)
+            if shadow is not None:      # float32 master, bf16 gradient widened, bf16 copy written
+                g = g.float()
             adamw_update_(p, g, m, v, lr=lr, beta1=beta1, beta2=beta2, eps=eps, weight_decay=weight_decay,
                           bias1=bias1, bias2=bias2)
+            if shadow is not None:
+                shadow.copy_(p.to(shadow.dtype))
 
     def muon(self, bucket, triples, *, adjust_lr_fn, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay,
              timer=None, reduce=None):
         copies = self._gather(reduce) if reduce is not None else None
-        for p, g, mom in triples:
+        for t in triples:
+            (p, g, mom), shadow = t[:3], (t[3] if len(t) > 3 else None)
             if reduce is not None:
                 g = reduced(g, copies, *reduce)
+            if shadow is not None:
+                g = g.float()
             muon_matrix_step_(p, g, mom, lr=lr, beta=beta, nesterov=nesterov, coeffs=(a, b, c), ns_steps=ns_steps,
                               eps=eps, weight_decay=weight_decay, adjust_lr_fn=adjust_lr_fn)
+            if shadow is not None:
+                shadow.copy_(p.to(shadow.dtype))
 
 
 def _make(seed=0, dtype=torch.float32):
@@ -153,13 +163,17 @@ def _worker(rank, world, port, mode, q):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
         from triton_muon_adamw import AdamConfig, MuonConfig
         from triton_muon_adamw.distributed import ShardedMuonAdamW
-        dtype = torch.bfloat16 if mode in ("bf16", "reduce_bf16") else torch.float32
+        dtype = torch.bfloat16 if mode in ("bf16", "reduce_bf16", "master") else torch.float32
         reduce = mode.startswith("reduce")
+        master = mode == "master"
         adam, muon = _make(dtype=dtype)
-        ref = OracleMuonAdamW([p.detach().clone() for p in adam], [p.detach().clone() for p in muon],
+        # Master mode: the reference is a float32 run on the masters with the bf16 gradients widened.
+        ref_dtype = torch.float32 if master else dtype
+        ref = OracleMuonAdamW([p.detach().to(ref_dtype) for p in adam], [p.detach().to(ref_dtype) for p in muon],
                               adam=ADAM, muon=MUON)
         opt = ShardedMuonAdamW(adam, muon, MuonConfig(**MUON), AdamConfig(**ADAM), dist.group.WORLD, n_buckets=2,
-                               backend=OracleBackend(), reduce_grads="mean" if reduce else None)
+                               backend=OracleBackend(), reduce_grads="mean" if reduce else None,
+                               master_weights=master)
         if mode == "die" and rank == 1:
             raise SystemExit(0)     # leaves before the first collective
         for step in range(2):
@@ -181,15 +195,23 @@ def _worker(rank, world, port, mode, q):
                 for p, g in zip(adam + muon, ga + gm):
                     p.grad = g.clone()
             opt.step()
+            if master:
+                ga, gm = [g.float() for g in ga], [g.float() for g in gm]
             ref.step(ga, gm)
         for p, r in zip(adam + muon, ref.params_adam + ref.params_muon):
-            assert p.dtype == dtype and torch.equal(p.detach(), r), f"rank {rank}: parameter {tuple(p.shape)} differs"
+            want = r.to(dtype) if master else r
+            assert p.dtype == dtype and torch.equal(p.detach(), want), f"rank {rank}: parameter {tuple(p.shape)} differs"
         sd = opt.state_dict()
         for i, (m, v) in enumerate(zip(ref.exp_avg, ref.exp_avg_sq)):
             assert torch.equal(sd["adam"]["state"][i]["exp_avg"], m)
             assert torch.equal(sd["adam"]["state"][i]["exp_avg_sq"], v)
         for i, mom in enumerate(ref.momentum):
             assert torch.equal(sd["muon"]["state"][i]["momentum_buffer"], mom)
+        if master:
+            for i, r in enumerate(ref.params_adam):
+                assert torch.equal(sd["adam"]["state"][i]["master_param"], r)
+            for i, r in enumerate(ref.params_muon):
+                assert torch.equal(sd["muon"]["state"][i]["master_param"], r)
         # round trip: zero the shards, load the gathered dict back, gather again
         opt.exp_avg.zero_()
         for t in opt.mom_segs:
@@ -234,6 +256,12 @@ def test_sharded_step_matches_single_process_oracle(world):
 def test_sharded_step_bf16_parameters():
     """bf16 parameters: bf16 flat buffers and momentum, float32 AdamW moment shards."""
     out = _run(2, "bf16")
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_sharded_step_master_weights():
+    """bf16 parameters with float32 masters on the owners: bit-identical to a float32 run on the masters."""
+    out = _run(2, "master")
     assert out == {0: "ok", 1: "ok"}, out
 
 

@@ -176,3 +176,45 @@ def test_muonadamw_bf16_vs_reference_wrapper_golden(cuda_device):
         for p, q in zip(params[:na], o.params_adam):
             _within_one_ulp(p.detach(), q, f"AdamW {tuple(p.shape)}")
     assert opt.device_status() == 0
+
+
+# ----------------------------------------------------------------- float32 masters
+def test_master_weights_match_float32_run_on_the_masters(cuda_device):
+    """master_weights=True: bf16 parameters and gradients, float32 masters and Muon momentum.
+
+    The masters must equal, bit for bit, a float32 MuonAdamW run whose
+    parameters start as the masters and whose gradients are the bf16 ones
+    widened; every bf16 parameter must be its master rounded to bf16.
+    """
+    from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+    gen = torch.Generator().manual_seed(17)
+    adam_shapes = [(300,), (64, 8), (1000,)]
+    muon_shapes = [(64, 96), (200, 72), (5, 3), (256, 256)]
+    init = [(torch.randn(s, generator=gen) * 0.02).to(torch.bfloat16) for s in adam_shapes + muon_shapes]
+    na = len(adam_shapes)
+    mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4, betas=(0.9, 0.95))
+    bf = [torch.nn.Parameter(t.clone().to(cuda_device)) for t in init]
+    f32 = [torch.nn.Parameter(t.float().to(cuda_device)) for t in init]
+    opt = MuonAdamW({"adam": bf[:na], "muon": bf[na:]}, muon_config=mc, adam_config=ac, parameter_split="explicit",
+                    master_weights=True)
+    ref = MuonAdamW({"adam": f32[:na], "muon": f32[na:]}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+    for _ in range(3):
+        grads = [(torch.randn(t.shape, generator=gen) * 1e-3).to(torch.bfloat16).to(cuda_device) for t in init]
+        for p, q, g in zip(bf, f32, grads):
+            p.grad, q.grad = g, g.float()
+        opt.step()
+        ref.step()
+    masters = {**opt.adamw.masters, **opt.muon.masters}
+    for p, q in zip(bf, f32):
+        assert torch.equal(masters[p], q.detach()), f"master {tuple(p.shape)}"
+        assert p.dtype == torch.bfloat16 and torch.equal(p.detach(), q.detach().to(torch.bfloat16)), tuple(p.shape)
+    sd = opt.state_dict()
+    assert torch.equal(sd["muon"]["state"][0]["master_param"], f32[na].detach())
+    assert opt.device_status() == 0
+
+
+def test_master_weights_need_bf16_parameters(cuda_device):
+    from triton_muon_adamw import MuonAdamW
+    p = torch.nn.Parameter(torch.zeros(8, 8, device=cuda_device))
+    with pytest.raises(TypeError):
+        MuonAdamW({"adam": [], "muon": [p]}, parameter_split="explicit", master_weights=True)

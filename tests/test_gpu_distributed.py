@@ -79,6 +79,47 @@ def _worker_reduce(rank, world, port, q, dtype):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
 
 
+def _worker_master(rank, world, port, q):
+    """master_weights=True sharded (bf16 exchange, float32 masters on the owners) vs single-GPU master mode."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+        mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4, betas=(0.9, 0.95))
+
+        def bf16_params():
+            adam, muon = _params(dev)
+            return ([torch.nn.Parameter(p.detach().to(torch.bfloat16)) for p in ps] for ps in (adam, muon))
+
+        adam, muon = bf16_params()
+        sharded = MuonAdamW({"adam": adam, "muon": muon}, muon_config=mc, adam_config=ac, parameter_split="explicit",
+                            process_group=dist.group.WORLD, master_weights=True)
+        adam1, muon1 = bf16_params()
+        single = MuonAdamW({"adam": adam1, "muon": muon1}, muon_config=mc, adam_config=ac,
+                           parameter_split="explicit", master_weights=True)
+        for step in range(3):
+            gs = [g.to(torch.bfloat16) for g in _grads(step, dev)]
+            for p, p1, g in zip(adam + muon, adam1 + muon1, gs):
+                p.grad, p1.grad = g.clone(), g.clone()
+            sharded.step()
+            single.step()
+        torch.cuda.synchronize()
+        for p, p1 in zip(adam + muon, adam1 + muon1):
+            assert torch.equal(p.detach(), p1.detach()), f"rank {rank}: {tuple(p.shape)} differs"
+        sd, ref = sharded.state_dict(), single.state_dict()
+        for br in ("adam", "muon"):
+            for i in ref[br]["state"]:
+                assert torch.equal(sd[br]["state"][i]["master_param"], ref[br]["state"][i]["master_param"]), (br, i)
+        sharded.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
 def _worker(rank, world, port, q):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -153,3 +194,11 @@ def test_fused_gradient_reduction(world, dtype):
         pytest.skip(f"needs {world} GPUs")
     out = _spawn(_worker_reduce, world, dtype)
     assert out == {r: "ok" for r in range(world)}, out
+
+
+def test_two_gpu_master_weights_sharded_step():
+    """bf16 parameters exchanged between ranks, float32 masters kept by their owners."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _spawn(_worker_master, 2)
+    assert out == {0: "ok", 1: "ok"}, out

@@ -128,8 +128,11 @@ def _buf(plan, i, which):
     return flat.view(rows, ld)[:, :cols]
 
 
+MATDESC_BYTES, INV_NORM_OFFSET = 136, 92     # sizeof(MatDesc), offsetof(MatDesc, inv_norm): csrc/plan.cuh
+
+
 def _inv_norm(plan, i):
-    off = plan.info.off_mats + i * 128 + 92      # MatDesc.inv_norm
+    off = plan.info.off_mats + i * MATDESC_BYTES + INV_NORM_OFFSET
     return float(plan.table[off:off + 4].view(torch.float32).item())
 
 

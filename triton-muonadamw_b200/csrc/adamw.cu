@@ -1,6 +1,7 @@
 // AdamW branch: one elementwise fp32 update of param, exp_avg, exp_avg_sq.
 // Parameters and gradients may be float32 or bf16 (moments always float32);
 // bf16 values are widened on load and rounded once, to nearest even, on store.
+// A float32 master parameter with a bf16 gradient also stores its bf16 copy.
 //
 // Follows the reference kernel's formula (triton_adam.py:53-63):
 //   m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g²
@@ -48,16 +49,27 @@ __device__ __forceinline__ void adam_vec(float4& p, const float4& g, float4& m, 
   adam_elem(p.w, g.w, m.w, v.w, s);
 }
 
-// One tile [off, off+len) of one tensor whose parameter and gradient have
-// element type T (the moments are float32).  Full aligned tiles take the
-// 16-loads-in-flight path; ragged or misaligned pieces take a generic loop.
+// Stores of an updated parameter vector: the parameter itself and, for a
+// float32 master (SHADOW), its bf16 copy rounded to nearest even.
+template <typename TP, bool SHADOW>
+__device__ __forceinline__ void put4(TP* p, __nv_bfloat16* sh, int64_t i, const float4& a) {
+  st4(p, i, a);
+  if (SHADOW) st4(sh, i, a);
+}
+template <typename TP, bool SHADOW>
+__device__ __forceinline__ void put1(TP* p, __nv_bfloat16* sh, int64_t i, float a) {
+  st1(p, i, a);
+  if (SHADOW) st1(sh, i, a);
+}
+
 // The tile with the gradient summed over ranks.  Full tiles: each thread's
 // four vectors of every rank's copy, two ranks (8 vectors) in flight at a
 // time, then p, m, v; the remote reads cross NVLink, which bounds this path.
-template <typename T>
+template <typename TP, typename TG, bool SHADOW>
 __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
-  T* __restrict__ p = static_cast<T*>(e.p) + off;
-  const T* g = static_cast<const T*>(e.g) + off;
+  TP* __restrict__ p = static_cast<TP*>(e.p) + off;
+  const TG* g = static_cast<const TG*>(e.g) + off;
+  __nv_bfloat16* __restrict__ sh = SHADOW ? static_cast<__nv_bfloat16*>(e.shadow) + off : nullptr;
   float* __restrict__ m = e.m + off;
   float* __restrict__ v = e.v + off;
   const int t = threadIdx.x;
@@ -66,7 +78,7 @@ __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off
     float4 gv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) offs[j] = 4 * static_cast<int64_t>(j * ADAM_THREADS + t);
-    ld4_ranks_rows<T, 4>(g, offs, gv, s.red);
+    ld4_ranks_rows<TG, 4>(g, offs, gv, s.red);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int idx = j * ADAM_THREADS + t;
@@ -74,7 +86,7 @@ __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off
       float4 c = __ldcs(reinterpret_cast<const float4*>(m) + idx);
       float4 d = __ldcs(reinterpret_cast<const float4*>(v) + idx);
       adam_vec(a, gv[j], c, d, s);
-      st4(p, idx, a);
+      put4<TP, SHADOW>(p, sh, idx, a);
       __stcs(reinterpret_cast<float4*>(m) + idx, c);
       __stcs(reinterpret_cast<float4*>(v) + idx, d);
     }
@@ -87,23 +99,27 @@ __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off
     float4 c = __ldcs(reinterpret_cast<const float4*>(m) + i);
     float4 d = __ldcs(reinterpret_cast<const float4*>(v) + i);
     adam_vec(a, b, c, d, s);
-    st4(p, i, a);
+    put4<TP, SHADOW>(p, sh, i, a);
     __stcs(reinterpret_cast<float4*>(m) + i, c);
     __stcs(reinterpret_cast<float4*>(v) + i, d);
   }
   for (int i = nvec * 4 + t; i < len; i += ADAM_THREADS) {
     float a = ld1(p, i), c = m[i], d = v[i];
     adam_elem(a, ld1_ranks(g, i, s.red), c, d, s);
-    st1(p, i, a);
+    put1<TP, SHADOW>(p, sh, i, a);
     m[i] = c;
     v[i] = d;
   }
 }
 
-template <typename T>
+// One tile [off, off+len) of one tensor: parameter type TP, gradient type TG,
+// float32 moments.  Full aligned tiles take the 16-loads-in-flight path;
+// ragged or misaligned pieces take a generic loop.
+template <typename TP, typename TG, bool SHADOW>
 __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
-  T* __restrict__ p = static_cast<T*>(e.p) + off;
-  const T* __restrict__ g = static_cast<const T*>(e.g) + off;
+  TP* __restrict__ p = static_cast<TP*>(e.p) + off;
+  const TG* __restrict__ g = static_cast<const TG*>(e.g) + off;
+  __nv_bfloat16* __restrict__ sh = SHADOW ? static_cast<__nv_bfloat16*>(e.shadow) + off : nullptr;
   float* __restrict__ m = e.m + off;
   float* __restrict__ v = e.v + off;
   const int t = threadIdx.x;
@@ -121,7 +137,7 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
     for (int i = 0; i < 4; ++i) {
       adam_vec(rp[i], rg[i], rm[i], rv[i], s);
       const int idx = i * ADAM_THREADS + t;
-      st4(p, idx, rp[i]);
+      put4<TP, SHADOW>(p, sh, idx, rp[i]);
       __stcs(reinterpret_cast<float4*>(m) + idx, rm[i]);
       __stcs(reinterpret_cast<float4*>(v) + idx, rv[i]);
     }
@@ -134,32 +150,35 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
     float4 c = __ldcs(reinterpret_cast<const float4*>(m) + i);
     float4 d = __ldcs(reinterpret_cast<const float4*>(v) + i);
     adam_vec(a, b, c, d, s);
-    st4(p, i, a);
+    put4<TP, SHADOW>(p, sh, i, a);
     __stcs(reinterpret_cast<float4*>(m) + i, c);
     __stcs(reinterpret_cast<float4*>(v) + i, d);
   }
   for (int i = nvec * 4 + t; i < len; i += ADAM_THREADS) {
     float a = ld1(p, i), c = m[i], d = v[i];
     adam_elem(a, ld1(g, i), c, d, s);
-    st1(p, i, a);
+    put1<TP, SHADOW>(p, sh, i, a);
     m[i] = c;
     v[i] = d;
   }
 }
 
+template <bool REDUCE, typename TP, typename TG, bool SHADOW>
+__device__ __forceinline__ void adam_tile_typed(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
+  if (REDUCE)
+    adam_tile_reduce<TP, TG, SHADOW>(e, off, len, s);
+  else
+    adam_tile<TP, TG, SHADOW>(e, off, len, s);
+}
+
 template <bool REDUCE>
 __device__ __forceinline__ void adam_tile_any(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
-  if (REDUCE) {
-    if (e.dtype == 1)
-      adam_tile_reduce<__nv_bfloat16>(e, off, len, s);
-    else
-      adam_tile_reduce<float>(e, off, len, s);
-  } else {
-    if (e.dtype == 1)
-      adam_tile<__nv_bfloat16>(e, off, len, s);
-    else
-      adam_tile<float>(e, off, len, s);
-  }
+  if (e.dtype == MAD_DTYPE_BF16)
+    adam_tile_typed<REDUCE, __nv_bfloat16, __nv_bfloat16, false>(e, off, len, s);
+  else if (e.dtype == MAD_DTYPE_F32_MASTER)
+    adam_tile_typed<REDUCE, float, __nv_bfloat16, true>(e, off, len, s);
+  else
+    adam_tile_typed<REDUCE, float, float, false>(e, off, len, s);
 }
 
 // REDUCE: the gradient summed over ranks (a separate instantiation, so the
@@ -214,9 +233,12 @@ static inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>
 
 // 4-element vectors are legal when p, g (4 elements: 16 B float32, 8 B bf16)
 // and the float32 moments (16 B) are aligned for them.
-static inline int32_t vec_ok(const void* p, const void* g, const float* m, const float* v, int32_t dtype) {
-  const bool pg = dtype == MAD_DTYPE_BF16 ? aligned8(p) && aligned8(g) : aligned16(p) && aligned16(g);
-  return pg && aligned16(m) && aligned16(v);
+static inline int32_t vec_ok(const void* p, const void* g, const float* m, const float* v, const void* shadow,
+                             int32_t dtype) {
+  if (dtype == MAD_DTYPE_BF16) return aligned8(p) && aligned8(g) && aligned16(m) && aligned16(v);
+  if (dtype == MAD_DTYPE_F32_MASTER)
+    return aligned16(p) && aligned8(g) && aligned8(shadow) && aligned16(m) && aligned16(v);
+  return aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v);
 }
 
 // Table layout: int32 tile map [n_tiles] at offset 0, then the AdamEntry array
@@ -250,7 +272,7 @@ extern "C" int mad_adamw_step(float* param, const float* grad, float* exp_avg, f
   e.numel = numel;
   e.tile_begin = 0;
   e.dtype = MAD_DTYPE_F32;
-  e.vec = vec_ok(param, grad, exp_avg, exp_avg_sq, MAD_DTYPE_F32);
+  e.vec = vec_ok(param, grad, exp_avg, exp_avg_sq, nullptr, MAD_DTYPE_F32);
   const int64_t n_tiles = (numel + ADAM_TILE - 1) / ADAM_TILE;
   adamw_single_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       e, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
@@ -282,8 +304,10 @@ extern "C" int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors
     if (t.numel < 0) return fail(MAD_ERR_INVALID, "mad_adamw_plan: negative numel");
     if (t.numel > 0 && (!t.param || !t.grad || !t.exp_avg || !t.exp_avg_sq))
       return fail(MAD_ERR_INVALID, "mad_adamw_plan: null pointer in tensor %d", i);
-    if (t.dtype != MAD_DTYPE_F32 && t.dtype != MAD_DTYPE_BF16)
+    if (t.dtype != MAD_DTYPE_F32 && t.dtype != MAD_DTYPE_BF16 && t.dtype != MAD_DTYPE_F32_MASTER)
       return fail(MAD_ERR_INVALID, "mad_adamw_plan: tensor %d has unknown dtype %d", i, t.dtype);
+    if (t.dtype == MAD_DTYPE_F32_MASTER && t.numel > 0 && !t.shadow)
+      return fail(MAD_ERR_INVALID, "mad_adamw_plan: tensor %d (float32 master) has no bf16 shadow", i);
     AdamEntry& e = entries[i];
     std::memset(&e, 0, sizeof(e));
     e.p = t.param;
@@ -293,7 +317,8 @@ extern "C" int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors
     e.numel = t.numel;
     e.tile_begin = tiles;
     e.dtype = t.dtype;
-    e.vec = vec_ok(t.param, t.grad, t.exp_avg, t.exp_avg_sq, t.dtype);
+    e.shadow = t.dtype == MAD_DTYPE_F32_MASTER ? t.shadow : nullptr;
+    e.vec = vec_ok(t.param, t.grad, t.exp_avg, t.exp_avg_sq, t.shadow, t.dtype);
     tiles += (t.numel + ADAM_TILE - 1) / ADAM_TILE;
   }
   if (tiles > INT32_MAX) return fail(MAD_ERR_INVALID, "mad_adamw_plan: too many tiles");

@@ -12,4 +12,4 @@ char* error_buffer() {
 
 extern "C" const char* mad_last_error(void) { return mad::error_buffer(); }
 
-extern "C" int32_t mad_abi_version(void) { return 3; }
+extern "C" int32_t mad_abi_version(void) { return 4; }

@@ -117,6 +117,8 @@ extern "C" int mad_muon_step_noalloc(float* param, const float* grad, float* mom
   mat.cols = cols;
   mat.lr_scale = lr_scale;
   mat.dtype = MAD_DTYPE_F32;
+  mat.pad = 0;
+  mat.shadow = nullptr;
   mad_muon_plan_info info;
   if (int rc = mad_muon_plan_size(&mat, 1, &info)) return rc;
   if (info.table_bytes > static_cast<int64_t>(NOALLOC_TABLE_BYTES) ||

@@ -36,11 +36,15 @@ inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 
-// 4-element vector access (16 B float32, 8 B bf16) to every row of p, g, mom.
+// 4-element vector access (16 B float32, 8 B bf16) to every row of p, g, mom (and the shadow).
 inline bool vec_ok(const mad_muon_matrix& mt) {
-  const bool al = mt.dtype == MAD_DTYPE_BF16
-                      ? aligned8(mt.param) && aligned8(mt.grad) && aligned8(mt.momentum)
-                      : aligned16(mt.param) && aligned16(mt.grad) && aligned16(mt.momentum);
+  bool al;
+  if (mt.dtype == MAD_DTYPE_BF16)
+    al = aligned8(mt.param) && aligned8(mt.grad) && aligned8(mt.momentum);
+  else if (mt.dtype == MAD_DTYPE_F32_MASTER)
+    al = aligned16(mt.param) && aligned8(mt.grad) && aligned16(mt.momentum) && aligned8(mt.shadow);
+  else
+    al = aligned16(mt.param) && aligned16(mt.grad) && aligned16(mt.momentum);
   return al && mt.cols % 4 == 0;
 }
 
@@ -122,8 +126,10 @@ int validate(const mad_muon_matrix* mats, int32_t n) {
     if (mt.rows > (1 << 24) || mt.cols > (1 << 24) || mt.rows * mt.cols > (int64_t(1) << 34))
       return fail(MAD_ERR_INVALID, "muon plan: matrix %d is too large", i);
     if (!mt.param || !mt.grad || !mt.momentum) return fail(MAD_ERR_INVALID, "muon plan: matrix %d has a null pointer", i);
-    if (mt.dtype != MAD_DTYPE_F32 && mt.dtype != MAD_DTYPE_BF16)
+    if (mt.dtype != MAD_DTYPE_F32 && mt.dtype != MAD_DTYPE_BF16 && mt.dtype != MAD_DTYPE_F32_MASTER)
       return fail(MAD_ERR_INVALID, "muon plan: matrix %d has unknown dtype %d", i, mt.dtype);
+    if (mt.dtype == MAD_DTYPE_F32_MASTER && !mt.shadow)
+      return fail(MAD_ERR_INVALID, "muon plan: matrix %d (float32 master) has no bf16 shadow", i);
   }
   return MAD_OK;
 }
@@ -226,6 +232,7 @@ extern "C" int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* 
     d.tmap_base = i * TMAPS_PER_MAT;
     d.vec = vec_ok(mt) ? 1 : 0;
     d.dtype = mt.dtype;
+    d.shadow = mt.dtype == MAD_DTYPE_F32_MASTER ? mt.shadow : nullptr;
     prep_begin += d.prep_count;
     CUtensorMap* t = tm + d.tmap_base;
     if (int rc = encode_bf16(t + TM_XK0, d.x[0], s.m, s.n, s.ld_x, 128)) return rc;

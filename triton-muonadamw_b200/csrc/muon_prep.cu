@@ -45,14 +45,16 @@ __device__ __forceinline__ float prep_update(float g, float& mom, const PrepScal
 }
 
 // Momentum update of one 64x64 tile; xv receives the (Nesterov) update u for
-// the thread's 4 rows x 4 consecutive columns, 0 outside the matrix.
-template <typename T, bool REDUCE>
+// the thread's 4 rows x 4 consecutive columns, 0 outside the matrix.  TM is
+// the momentum's type (bf16 momentum rounds the glue to bf16), TG the
+// gradient's (a float32 master takes a bf16 gradient).
+template <typename TM, typename TG, bool REDUCE>
 __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, bool full, float (&xv)[4][4],
                                             const PrepScalars& s) {
-  constexpr bool BF16 = sizeof(T) == 2;
+  constexpr bool BF16 = sizeof(TM) == 2;
   const int rows = md->rows, cols = md->cols, t = threadIdx.x;
-  const T* __restrict__ g = static_cast<const T*>(md->g);
-  T* __restrict__ mom = static_cast<T*>(md->mom);
+  const TG* __restrict__ g = static_cast<const TG*>(md->g);
+  TM* __restrict__ mom = static_cast<TM*>(md->mom);
   const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
   if (full) {
     // All loads of the tile first (8 vectors in flight per thread), then compute and store.
@@ -65,7 +67,7 @@ __device__ __forceinline__ void prep_values(const MatDesc* md, int r0, int c0, b
         offs[i] = static_cast<int64_t>(r0 + i * 16 + (t >> 4)) * cols + c0 + cl;
         mv[i] = ld4(mom + offs[i], 0);
       }
-      ld4_ranks_rows<T, 4>(g, offs, gv, s.red);
+      ld4_ranks_rows<TG, 4>(g, offs, gv, s.red);
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -129,10 +131,12 @@ __global__ void __launch_bounds__(PREP_THREADS, REDUCE ? 2 : 4) muon_prep_kernel
     float ss = 0.f;
     const int cl = (t & 15) * 4;  // 4 consecutive columns per thread
     float xv[4][4];
-    if (md->dtype == 1)
-      prep_values<__nv_bfloat16, REDUCE>(md, r0, c0, full, xv, s);
+    if (md->dtype == MAD_DTYPE_BF16)
+      prep_values<__nv_bfloat16, __nv_bfloat16, REDUCE>(md, r0, c0, full, xv, s);
+    else if (md->dtype == MAD_DTYPE_F32_MASTER)
+      prep_values<float, __nv_bfloat16, REDUCE>(md, r0, c0, full, xv, s);
     else
-      prep_values<float, REDUCE>(md, r0, c0, full, xv, s);
+      prep_values<float, float, REDUCE>(md, r0, c0, full, xv, s);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int rl = i * 16 + (t >> 4);

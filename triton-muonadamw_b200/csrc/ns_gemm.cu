@@ -310,21 +310,24 @@ __device__ __forceinline__ float param_new(float p, float x, float slr, float lr
 }
 
 // Parameter write of one epilogue row chunk (32 columns of X' row `grow`), in
-// pieces of CW columns (16 for float32, 8 for bf16, whose longer rounding
-// chain needs more registers): within a piece all loads are issued before any
+// pieces of CW columns (16 for float32; 8 for bf16, whose longer rounding
+// chain needs more registers, and for a float32 master, which also stores its
+// bf16 shadow): within a piece all loads are issued before any
 // store (a store could otherwise alias a later load and serialise the chunk).
-template <typename T>
+template <typename T, bool SHADOW>
 __device__ __forceinline__ void write_params(const MatDesc& md, const float (&v)[32], int grow, int gcol0, int m,
                                              float slr, float lr_wd) {
-  constexpr int CW = sizeof(T) == 2 ? 8 : 16;
+  constexpr int CW = (sizeof(T) == 2 || SHADOW) ? 8 : 16;
   const int n = md.n;
   T* __restrict__ p = static_cast<T*>(md.p);
+  __nv_bfloat16* __restrict__ sh = SHADOW ? static_cast<__nv_bfloat16*>(md.shadow) : nullptr;
 #pragma unroll
   for (int h = 0; h < 32 / CW; ++h) {
     const int c0 = gcol0 + CW * h;
     float pv[CW];
     if (!md.transposed) {
-      T* prow = p + static_cast<int64_t>(grow) * n + c0;
+      const int64_t rbase = static_cast<int64_t>(grow) * n + c0;
+      T* prow = p + rbase;
       const bool vec = md.vec && c0 + CW <= n;
       if (vec) {
 #pragma unroll
@@ -343,23 +346,33 @@ __device__ __forceinline__ void write_params(const MatDesc& md, const float (&v)
       for (int k = 0; k < CW; ++k) pv[k] = param_new<T>(pv[k], v[CW * h + k], slr, lr_wd);
       if (vec) {
 #pragma unroll
-        for (int q = 0; q < CW / 4; ++q)
-          st4(prow, q, make_float4(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]));
+        for (int q = 0; q < CW / 4; ++q) {
+          const float4 w = make_float4(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
+          st4(prow, q, w);
+          if (SHADOW) st4(sh + rbase, q, w);
+        }
       } else {
 #pragma unroll
         for (int k = 0; k < CW; ++k)
-          if (c0 + k < n) st1(prow, k, pv[k]);
+          if (c0 + k < n) {
+            st1(prow, k, pv[k]);
+            if (SHADOW) st1(sh + rbase, k, pv[k]);
+          }
       }
     } else {
       // Parameter is n x m: X'[grow][col] lives at p[col][grow]; per k a warp touches 32 contiguous elements.
-      T* pcol = p + static_cast<int64_t>(c0) * m + grow;
+      const int64_t cbase = static_cast<int64_t>(c0) * m + grow;
+      T* pcol = p + cbase;
 #pragma unroll
       for (int k = 0; k < CW; ++k) pv[k] = (c0 + k < n) ? ld1(pcol, static_cast<int64_t>(k) * m) : 0.f;
 #pragma unroll
       for (int k = 0; k < CW; ++k) pv[k] = param_new<T>(pv[k], v[CW * h + k], slr, lr_wd);
 #pragma unroll
       for (int k = 0; k < CW; ++k)
-        if (c0 + k < n) st1(pcol, static_cast<int64_t>(k) * m, pv[k]);
+        if (c0 + k < n) {
+          st1(pcol, static_cast<int64_t>(k) * m, pv[k]);
+          if (SHADOW) st1(sh + cbase, static_cast<int64_t>(k) * m, pv[k]);
+        }
     }
   }
 }
@@ -395,10 +408,12 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
   if (!row_ok) return;
   // scaled_lr = lr * shape factor, formed in double and rounded once (triton_muon.py:424-431).
   const float slr = static_cast<float>(args.lr * md.lr_scale);
-  if (md.dtype == 1)
-    write_params<__nv_bfloat16>(md, v, grow, gcol0, m, slr, args.lr_wd);
+  if (md.dtype == MAD_DTYPE_BF16)
+    write_params<__nv_bfloat16, false>(md, v, grow, gcol0, m, slr, args.lr_wd);
+  else if (md.dtype == MAD_DTYPE_F32_MASTER)
+    write_params<float, true>(md, v, grow, gcol0, m, slr, args.lr_wd);
   else
-    write_params<float>(md, v, grow, gcol0, m, slr, args.lr_wd);
+    write_params<float, false>(md, v, grow, gcol0, m, slr, args.lr_wd);
 }
 
 // Eight epilogue warps: warp w reads TMEM lanes 32*(w%4).. (the hardware

@@ -17,16 +17,17 @@ namespace mad {
 // One tensor of the multi-tensor AdamW launch.  `vec` is 1 when every pointer
 // is 16-byte aligned, so 4-element vector loads/stores are legal.
 struct AdamEntry {
-  void* p;             // parameter, element type `dtype`
-  const void* g;       // gradient, element type `dtype`
+  void* p;             // parameter: float32, or bf16 for dtype 1
+  const void* g;       // gradient: float32 for dtype 0, else bf16
   float* m;
   float* v;
   int64_t numel;
   int64_t tile_begin;  // first global tile index of this tensor
   int32_t vec;
-  int32_t dtype;       // 0 float32, 1 bf16
+  int32_t dtype;       // MAD_DTYPE_*: 0 float32, 1 bf16, 2 float32 master + bf16 grad/shadow
+  void* shadow;        // dtype 2: bf16 copy of the updated parameter
 };
-static_assert(sizeof(AdamEntry) == 56, "AdamEntry layout");
+static_assert(sizeof(AdamEntry) == 64, "AdamEntry layout");
 
 constexpr int ADAM_THREADS = 256;
 constexpr int ADAM_TILE = 4096;  // elements per tile: 256 threads x 4 float4
@@ -48,9 +49,9 @@ constexpr int TMAPS_PER_MAT = 10;
 constexpr int PREP_TILE = 64;  // prep works on 64x64 tiles of the parameter
 
 struct MatDesc {
-  void* p;               // parameter, rows x cols, row-major, element type `dtype`
-  const void* g;         // gradient, same layout and type
-  void* mom;             // momentum buffer, same layout and type
+  void* p;               // parameter, rows x cols, row-major: float32, or bf16 for dtype 1
+  const void* g;         // gradient, same layout: float32 for dtype 0, else bf16
+  void* mom;             // momentum buffer, same layout and type as p
   __nv_bfloat16* x[2];   // Newton-Schulz iterate, m x n (ld_x), ping-pong
   __nv_bfloat16* gram;   // A, m x m (ld_mm)
   __nv_bfloat16* poly;   // B, m x m (ld_mm)
@@ -65,11 +66,12 @@ struct MatDesc {
   int32_t prep_count;    // number of prep tiles
   uint32_t done;         // prep tiles finished this step (reset by the last one)
   int32_t tmap_base;     // index of this matrix's first tensor map
-  int32_t vec;           // p, g, mom 16-byte aligned and cols % (16 / element size) == 0
-  int32_t dtype;         // 0 float32, 1 bf16
+  int32_t vec;           // 4-element vectors legal for p, g, mom (and shadow) on every row
+  int32_t dtype;         // MAD_DTYPE_*: 0 float32, 1 bf16, 2 float32 master + bf16 grad/shadow
   int32_t pad;
+  void* shadow;          // dtype 2: bf16 copy of the updated parameter, same layout as p
 };
-static_assert(sizeof(MatDesc) == 128, "MatDesc layout");
+static_assert(sizeof(MatDesc) == 136, "MatDesc layout");
 
 struct TileRef {
   int32_t mat;

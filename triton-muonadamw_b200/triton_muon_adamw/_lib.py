@@ -12,8 +12,8 @@ import os
 from pathlib import Path
 
 LIB_NAME = "libmuonadamw_b200.so"
-ABI_VERSION = 3  # mad_abi_version() of the library these structures describe
-DTYPE_F32, DTYPE_BF16 = 0, 1  # MAD_DTYPE_*
+ABI_VERSION = 4  # mad_abi_version() of the library these structures describe
+DTYPE_F32, DTYPE_BF16, DTYPE_F32_MASTER = 0, 1, 2  # MAD_DTYPE_*
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 c_int32 = ctypes.c_int32
@@ -24,12 +24,13 @@ c_void_p = ctypes.c_void_p
 
 class AdamWTensor(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("exp_avg", c_void_p), ("exp_avg_sq", c_void_p),
-                ("numel", c_int64), ("dtype", c_int32)]
+                ("numel", c_int64), ("dtype", c_int32), ("pad", c_int32), ("shadow", c_void_p)]
 
 
 class MuonMatrix(ctypes.Structure):
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("momentum", c_void_p), ("rows", c_int64),
-                ("cols", c_int64), ("lr_scale", ctypes.c_double), ("dtype", c_int32)]
+                ("cols", c_int64), ("lr_scale", ctypes.c_double), ("dtype", c_int32), ("pad", c_int32),
+                ("shadow", c_void_p)]
 
 
 class MuonPlanInfo(ctypes.Structure):

@@ -45,10 +45,21 @@ def _check_tensor(p: torch.Tensor, what: str, dtype: torch.dtype | None = None) 
         raise ValueError(f"{what} must be contiguous")
 
 
-class AdamWTable:
-    """Device tile table over a list of (param, grad, exp_avg, exp_avg_sq) views.
+def entry_dtype(p: torch.Tensor, g: torch.Tensor, shadow, what: str) -> int:
+    """C-ABI dtype of one (param, grad[, shadow]) entry: F32, BF16, or a float32 master with bf16 grad/shadow."""
+    if shadow is not None:
+        if p.dtype != torch.float32 or g.dtype != torch.bfloat16 or shadow.dtype != torch.bfloat16:
+            raise TypeError(f"{what}: a master entry needs a float32 master and bf16 gradient and shadow")
+        return _lib.DTYPE_F32_MASTER
+    return dtype_code(p, what)
 
-    param and grad share one dtype (float32 or bf16); the moments are float32.
+
+class AdamWTable:
+    """Device tile table over a list of (param, grad, exp_avg, exp_avg_sq[, shadow]) views.
+
+    param and grad share one dtype (float32 or bf16), or param is a float32
+    master with a bf16 grad and a bf16 shadow (the model's parameter, written
+    with the update); the moments are float32.
     """
 
     def __init__(self):
@@ -58,15 +69,17 @@ class AdamWTable:
         self.numel = 0
 
     def ensure(self, quads, device) -> None:
-        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), p.dtype)
-                    for p, g, m, v in quads)
+        quads = [tuple(q) + (None,) * (5 - len(q)) for q in quads]
+        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), p.dtype,
+                     sh.data_ptr() if sh is not None else 0) for p, g, m, v, sh in quads)
         if key == self.key:
             return
         lib = _lib.load()
         arr = (_lib.AdamWTensor * max(1, len(quads)))()
-        for i, (p, g, m, v) in enumerate(quads):
+        for i, (p, g, m, v, sh) in enumerate(quads):
             arr[i] = _lib.AdamWTensor(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(),
-                                      dtype_code(p, "AdamW parameter"))
+                                      entry_dtype(p, g, sh, "AdamW parameter"), 0,
+                                      sh.data_ptr() if sh is not None else None)
         nbytes = ctypes.c_int64()
         _lib.check(lib.mad_adamw_table_bytes(arr, len(quads), ctypes.byref(nbytes)), "mad_adamw_table_bytes")
         self.table = torch.empty(max(1, nbytes.value), dtype=torch.uint8, device=device)
@@ -74,7 +87,7 @@ class AdamWTable:
         _lib.check(lib.mad_adamw_plan(arr, len(quads), self.table.data_ptr(), nbytes.value, ctypes.byref(n_tiles),
                                       _lib.stream_handle()), "mad_adamw_plan")
         self.n_tiles = n_tiles.value
-        self.numel = sum(p.numel() for p, _, _, _ in quads)
+        self.numel = sum(q[0].numel() for q in quads)
         self.key = key
 
     def launch(self, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, reduce=None) -> None:
@@ -119,6 +132,7 @@ class TritonAdamW:
         for param in self.model_params:
             self.m[param] = torch.zeros_like(param, dtype=torch.float32)
             self.v[param] = torch.zeros_like(param, dtype=torch.float32)
+        self.masters = None  # {param: float32 master} in mixed-precision mode (MuonAdamW(master_weights=True))
         self._table = AdamWTable()
 
     def _active(self):
@@ -128,7 +142,10 @@ class TritonAdamW:
                 continue
             _check_tensor(p, "AdamW parameter")
             _check_tensor(p.grad, "AdamW gradient", p.dtype)
-            quads.append((p.data, p.grad, self.m[p], self.v[p]))
+            if self.masters is not None:
+                quads.append((self.masters[p], p.grad, self.m[p], self.v[p], p.data))
+            else:
+                quads.append((p.data, p.grad, self.m[p], self.v[p]))
         return quads
 
     @torch.no_grad()

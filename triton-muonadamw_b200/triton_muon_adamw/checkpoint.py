@@ -7,7 +7,8 @@ entries indexed by position in each branch's parameter list:
 * Muon:  ``{"momentum_buffer": ...}``
 
 plus one ``param_groups`` entry per branch carrying the hyperparameters under
-torch's names.  A dict saved by ``PyTorchMuonAdamW`` loads here and vice
+torch's names.  With ``master_weights=True`` each entry also holds the float32
+master of its (bf16) parameter under ``"master_param"``.  A dict saved by ``PyTorchMuonAdamW`` loads here and vice
 versa.  For compatibility with the reference's ``load_state_dict``
 (optimizer.py:170-175), a branch given as a plain parameter list replaces that
 branch's parameter list (new parameters get zero state).
@@ -42,18 +43,29 @@ def branch_state_dicts(opt) -> dict:
         for i, p in enumerate(ad.model_params):
             adam_state[i] = {"step": torch.tensor(float(ad.step_num), dtype=torch.float32, device=p.device),
                              "exp_avg": ad.m[p], "exp_avg_sq": ad.v[p]}
+            if ad.masters is not None:
+                adam_state[i]["master_param"] = ad.masters[p]
     muon_state = {i: {"momentum_buffer": mu.momentum[p]} for i, p in enumerate(mu.model_params)}
+    if mu.masters is not None:
+        for i, p in enumerate(mu.model_params):
+            muon_state[i]["master_param"] = mu.masters[p]
     return {"adam": {"state": adam_state, "param_groups": [_adam_group(ad, len(ad.model_params))]},
             "muon": {"state": muon_state, "param_groups": [_muon_group(mu, len(mu.model_params))]}}
 
 
 def _replace_params(branch, params, states):
     branch.model_params = list(params)
+    masters = getattr(branch, "masters", None)
     for name in states:
         store = getattr(branch, name)
         for p in branch.model_params:
             if p not in store:
-                store[p] = torch.zeros_like(p, dtype=torch.float32 if name in ("m", "v") else p.dtype)
+                fp32 = name in ("m", "v") or masters is not None   # master mode: float32 momentum
+                store[p] = torch.zeros_like(p, dtype=torch.float32 if fp32 else p.dtype)
+    if masters is not None:
+        for p in branch.model_params:
+            if p not in masters:
+                masters[p] = p.detach().float()
 
 
 @torch.no_grad()
@@ -76,6 +88,8 @@ def load_branch_state_dicts(opt, sd: dict) -> None:
                     continue
                 ad.m[p].copy_(st["exp_avg"])
                 ad.v[p].copy_(st["exp_avg_sq"])
+                if ad.masters is not None:
+                    ad.masters[p].copy_(st["master_param"] if "master_param" in st else p.detach().float())
                 steps.append(int(float(st["step"])))
             ad.step_num = max(steps) if steps else 0
     if "muon" in sd:
@@ -93,4 +107,7 @@ def load_branch_state_dicts(opt, sd: dict) -> None:
                 st = m["state"].get(i)
                 if st is not None and "momentum_buffer" in st:
                     mu.momentum[p].copy_(st["momentum_buffer"])
+                if mu.masters is not None:
+                    mu.masters[p].copy_(st["master_param"] if st is not None and "master_param" in st
+                                        else p.detach().float())
     opt.param_group = {"adam": ad.model_params, "muon": mu.model_params}

@@ -315,7 +315,7 @@ class ShardedMuonAdamW:
     """The MuonAdamW step partitioned over a process group (see the module docstring)."""
 
     def __init__(self, adam_params, muon_params, muon_config, adam_config, process_group, *, n_buckets=5,
-                 backend=None, reduce_grads=None):
+                 backend=None, reduce_grads=None, master_weights=False):
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
         if muon_config.adjust_lr_fn not in ADJUST_LR_FNS:
@@ -327,8 +327,13 @@ class ShardedMuonAdamW:
         if len(dtypes) > 1 or not dtypes <= {torch.float32, torch.bfloat16}:
             raise TypeError(f"sharded parameters must all be float32 or all bfloat16, got {sorted(map(str, dtypes))}")
         # Parameters and Muon momentum live in flat buffers of the parameters' dtype;
-        # the AdamW moments are float32.
+        # the AdamW moments are float32.  With master_weights the parameters are bf16
+        # and each rank keeps float32 masters (and float32 momentum) of what it owns.
         self.dtype = dtypes.pop() if dtypes else torch.float32
+        self.master_weights = bool(master_weights)
+        if self.master_weights and self.dtype != torch.bfloat16:
+            raise TypeError("master_weights=True needs bfloat16 parameters")
+        mom_dtype = torch.float32 if self.master_weights else self.dtype
         self.pg = process_group
         self.rank = dist.get_rank(process_group)
         self.world = dist.get_world_size(process_group)
@@ -378,7 +383,13 @@ class ShardedMuonAdamW:
                 view.copy_(p.data)
                 p.data = view
         # Momentum for owned matrices, laid out like the owner's parameter segment.
-        self.mom_segs = [torch.zeros(seg, dtype=self.dtype, device=self.device) for seg in self.seg_sizes]
+        self.mom_segs = [torch.zeros(seg, dtype=mom_dtype, device=self.device) for seg in self.seg_sizes]
+        # float32 masters of what this rank owns: its AdamW range and its Muon segments.
+        self.adam_master, self.master_segs = None, []
+        if self.master_weights:
+            self.adam_master = self.adam_flat[lo:lo + self.adam_shard].float()
+            self.master_segs = [f[self.rank * seg:(self.rank + 1) * seg].float()
+                                for f, seg in zip(self.muon_flats, self.seg_sizes)]
         mu.momentum = {}
         for p, s in zip(mu.model_params, self.slots):
             if s.owner == self.rank:
@@ -466,8 +477,12 @@ class ShardedMuonAdamW:
             if p.grad is None:
                 continue
             o = self.adam_offsets[i] + start
-            quads.append((self.adam_flat[o:o + length], p.grad.reshape(-1)[start:start + length],
-                          self.exp_avg[sh:sh + length], self.exp_avg_sq[sh:sh + length]))
+            piece = self.adam_flat[o:o + length]
+            g, m, v = p.grad.reshape(-1)[start:start + length], self.exp_avg[sh:sh + length], self.exp_avg_sq[sh:sh + length]
+            if self.master_weights:
+                quads.append((self.adam_master[sh:sh + length], g, m, v, piece))
+            else:
+                quads.append((piece, g, m, v))
         return quads
 
     def _bucket_triples(self, b):
@@ -475,7 +490,12 @@ class ShardedMuonAdamW:
         out = []
         for p, s in zip(mu.model_params, self.slots):
             if s.bucket == b and s.owner == self.rank and p.grad is not None and p.numel() > 0:
-                out.append((p.data, p.grad, mu.momentum[p]))
+                if self.master_weights:
+                    o = s.offset - self.rank * self.seg_sizes[b]
+                    master = self.master_segs[b][o:o + s.numel].view_as(p)
+                    out.append((master, p.grad, mu.momentum[p], p.data))
+                else:
+                    out.append((p.data, p.grad, mu.momentum[p]))
         return out
 
     def _gather(self, flat: torch.Tensor, seg: int):
@@ -590,6 +610,10 @@ class ShardedMuonAdamW:
         full_v = torch.empty_like(full_m)
         dist.all_gather_into_tensor(full_m, self.exp_avg, group=self.pg)
         dist.all_gather_into_tensor(full_v, self.exp_avg_sq, group=self.pg)
+        full_master = None
+        if self.master_weights:
+            full_master = torch.empty_like(full_m)
+            dist.all_gather_into_tensor(full_master, self.adam_master, group=self.pg)
         adam_state = {}
         if ad.step_num > 0:
             for i, p in enumerate(ad.model_params):
@@ -597,13 +621,24 @@ class ShardedMuonAdamW:
                 adam_state[i] = {"step": torch.tensor(float(ad.step_num), dtype=torch.float32, device=p.device),
                                  "exp_avg": full_m[o:o + n].view_as(p).clone(),
                                  "exp_avg_sq": full_v[o:o + n].view_as(p).clone()}
-        fulls = []
-        for seg, mom in zip(self.seg_sizes, self.mom_segs):
-            f = torch.empty(seg * self.world, dtype=self.dtype, device=self.device)
-            dist.all_gather_into_tensor(f, mom, group=self.pg)
-            fulls.append(f)
+                if full_master is not None:
+                    adam_state[i]["master_param"] = full_master[o:o + n].view_as(p).clone()
+
+        def gather(parts):
+            out = []
+            for seg, t in zip(self.seg_sizes, parts):
+                f = torch.empty(seg * self.world, dtype=t.dtype, device=self.device)
+                dist.all_gather_into_tensor(f, t, group=self.pg)
+                out.append(f)
+            return out
+
+        fulls = gather(self.mom_segs)
         muon_state = {i: {"momentum_buffer": fulls[s.bucket][s.offset:s.offset + s.numel].view_as(p).clone()}
                       for i, (p, s) in enumerate(zip(mu.model_params, self.slots))}
+        if self.master_weights:
+            masters = gather(self.master_segs)
+            for i, (p, s) in enumerate(zip(mu.model_params, self.slots)):
+                muon_state[i]["master_param"] = masters[s.bucket][s.offset:s.offset + s.numel].view_as(p).clone()
         return {"adam": {"state": adam_state, "param_groups": [_adam_group(ad, len(ad.model_params))]},
                 "muon": {"state": muon_state, "param_groups": [_muon_group(mu, len(mu.model_params))]}}
 
@@ -622,6 +657,8 @@ class ShardedMuonAdamW:
                     continue
                 self.exp_avg[sh:sh + length].copy_(st["exp_avg"].reshape(-1)[start:start + length])
                 self.exp_avg_sq[sh:sh + length].copy_(st["exp_avg_sq"].reshape(-1)[start:start + length])
+                if self.master_weights and "master_param" in st:
+                    self.adam_master[sh:sh + length].copy_(st["master_param"].reshape(-1)[start:start + length])
             for st in a["state"].values():
                 steps.append(int(float(st["step"])))
             ad.step_num = max(steps) if steps else 0
@@ -633,10 +670,13 @@ class ShardedMuonAdamW:
                 mu.a, mu.b, mu.c = g["ns_coefficients"]
             mu.eps, mu.steps = g.get("eps", mu.eps), g.get("ns_steps", mu.steps)
             mu.adjust_lr_fn = g.get("adjust_lr_fn") or "original"
-            for i, p in enumerate(mu.model_params):
+            for i, (p, s) in enumerate(zip(mu.model_params, self.slots)):
                 st = m["state"].get(i)
                 if st is not None and p in mu.momentum:
                     mu.momentum[p].copy_(st["momentum_buffer"])
+                    if self.master_weights and "master_param" in st:
+                        o = s.offset - self.rank * self.seg_sizes[s.bucket]
+                        self.master_segs[s.bucket][o:o + s.numel].copy_(st["master_param"].reshape(-1))
 
 
 __all__ = ["ShardedMuonAdamW", "CudaBackend", "lpt_assign", "split_buckets", "muon_layout", "zero1_layout",

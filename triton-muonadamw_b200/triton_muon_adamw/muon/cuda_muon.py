@@ -25,7 +25,7 @@ import torch
 import torch.nn as nn
 
 from .. import _lib
-from ..adamw.cuda_adam import dtype_code
+from ..adamw.cuda_adam import dtype_code, entry_dtype
 
 ADJUST_LR_FNS = ("original", "match_rms_adamw", "spectral_unclamped")
 
@@ -45,7 +45,11 @@ def lr_scale(shape, adjust_lr_fn: str) -> float:
 
 
 class MuonPlan:
-    """Device plan for a fixed list of (param, grad, momentum) matrices, each float32 or bf16."""
+    """Device plan for a fixed list of (param, grad, momentum[, shadow]) matrices.
+
+    Each matrix is float32 or bf16 throughout, or a float32 master (and
+    momentum) with a bf16 grad and a bf16 shadow written with the update.
+    """
 
     def __init__(self):
         self.key = None
@@ -57,16 +61,18 @@ class MuonPlan:
         self.shapes = []
 
     def ensure(self, triples, adjust_lr_fn, device) -> None:
-        key = (adjust_lr_fn,) + tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), tuple(p.shape), p.dtype)
-                                      for p, g, m in triples)
+        triples = [tuple(t) + (None,) * (4 - len(t)) for t in triples]
+        key = (adjust_lr_fn,) + tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), tuple(p.shape), p.dtype,
+                                       sh.data_ptr() if sh is not None else 0) for p, g, m, sh in triples)
         if key == self.key:
             return
         lib = _lib.load()
         n = len(triples)
         arr = (_lib.MuonMatrix * max(1, n))()
-        for i, (p, g, m) in enumerate(triples):
+        for i, (p, g, m, sh) in enumerate(triples):
             arr[i] = _lib.MuonMatrix(p.data_ptr(), g.data_ptr(), m.data_ptr(), p.shape[0], p.shape[1],
-                                     lr_scale(p.shape, adjust_lr_fn), dtype_code(p, "Muon parameter"))
+                                     lr_scale(p.shape, adjust_lr_fn), entry_dtype(p, g, sh, "Muon parameter"), 0,
+                                     sh.data_ptr() if sh is not None else None)
         info = _lib.MuonPlanInfo()
         _lib.check(lib.mad_muon_plan_size(arr, n, ctypes.byref(info)), "mad_muon_plan_size")
         self.table = torch.empty(max(1, info.table_bytes), dtype=torch.uint8, device=device)
@@ -81,7 +87,7 @@ class MuonPlan:
         self.info = info
         self.buffers = bufs
         self.n_mats = n
-        self.shapes = [tuple(p.shape) for p, _, _ in triples]
+        self.shapes = [tuple(t[0].shape) for t in triples]
         self.key = key
 
     def read_status(self, clear=True) -> int:
@@ -168,6 +174,7 @@ class TritonMuon:
         self.momentum = {}
         for param in self.model_params:
             self.momentum[param] = torch.zeros_like(param, device=param.device, dtype=param.dtype)
+        self.masters = None  # {param: float32 master} in mixed-precision mode (MuonAdamW(master_weights=True))
         self._plan = MuonPlan()
 
     def _active(self, only=None):
@@ -177,7 +184,7 @@ class TritonMuon:
                 continue
             if p.ndim != 2:
                 raise AssertionError("Muon only supports 2D tensors")
-            for t, what in ((p, "Muon parameter"), (p.grad, "Muon gradient"), (self.momentum[p], "Muon momentum")):
+            for t, what in ((p, "Muon parameter"), (p.grad, "Muon gradient")):
                 if not t.is_cuda:
                     raise ValueError(f"{what} must be a CUDA tensor (this optimizer runs only on the GPU)")
                 dtype_code(t, what)
@@ -187,7 +194,10 @@ class TritonMuon:
                     raise ValueError(f"{what} must be contiguous")
             if p.numel() == 0:
                 continue
-            triples.append((p.data, p.grad, self.momentum[p]))
+            if self.masters is not None:
+                triples.append((self.masters[p], p.grad, self.momentum[p], p.data))
+            else:
+                triples.append((p.data, p.grad, self.momentum[p]))
         return triples
 
     @torch.no_grad()

@@ -162,6 +162,15 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         segment into the others' replicas with ``cudaMemcpyAsync``, no SM),
         ``"kernel"`` (a small broadcast kernel beside the GEMMs) or
         ``"hybrid"`` (copy engines and kernel, half each).
+    master_weights:
+        Mixed precision: the parameters (and their gradients) are bfloat16 and
+        the optimizer keeps a float32 master copy of each, with float32 Muon
+        momentum.  Every update runs on the master in float32, as for float32
+        parameters, and writes the bf16 parameter with the same store; the
+        master and the update are what a float32 run on the masters with the
+        bf16 gradients would give, bit for bit.  Sharded, each rank keeps the
+        masters of what it owns and the all-gather moves bf16 (half the bytes).
+        Checkpoints carry the masters (``"master_param"`` per parameter).
     """
 
     def __init__(
@@ -173,16 +182,21 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         process_group=None,
         reduce_grads: Literal["mean", "sum"] | None = None,
         peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid"] = "auto",
+        master_weights: bool = False,
     ) -> None:
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
         adam_params, muon_params = split_parameters(model_params, parameter_split)
+        self.master_weights = bool(master_weights)
+        if self.master_weights and any(p.dtype != torch.bfloat16 for p in adam_params + muon_params):
+            raise TypeError("master_weights=True needs bfloat16 parameters (the masters are float32)")
         self.process_group = process_group
         self.distributed = None
         if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
             from .distributed import CudaBackend, ShardedMuonAdamW  # noqa: PLC0415
             self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group,
-                                                reduce_grads=reduce_grads, backend=CudaBackend(push=peer_push))
+                                                reduce_grads=reduce_grads, backend=CudaBackend(push=peer_push),
+                                                master_weights=self.master_weights)
             self.adamw = self.distributed.adamw
             self.muon = self.distributed.muon
         else:
@@ -192,6 +206,11 @@ class MuonAdamW(TritonMuon, TritonAdamW):
                                    eps=muon_config.eps, weight_decay=muon_config.weight_decay,
                                    coeffs=muon_config.coeffs, nesterov=muon_config.nesterov,
                                    ns_steps=muon_config.ns_steps, adjust_lr_fn=muon_config.adjust_lr_fn)
+            if self.master_weights:
+                with torch.no_grad():
+                    self.adamw.masters = {p: p.detach().float() for p in self.adamw.model_params}
+                    self.muon.masters = {p: p.detach().float() for p in self.muon.model_params}
+                    self.muon.momentum = {p: torch.zeros_like(p, dtype=torch.float32) for p in self.muon.model_params}
         self.param_group = {
             "adam": self.adamw.model_params,
             "muon": self.muon.model_params,
