@@ -127,6 +127,18 @@ def test_lpt_balances_ns_cost():
         assert owner == lpt_assign(costs, n)          # deterministic on every rank
 
 
+def test_split_buckets_increasing_and_decreasing():
+    """Decreasing buckets (the sharded exchange) and increasing ones (the host-gradient pipeline)."""
+    from triton_muon_adamw.distributed import split_buckets
+    costs = [1.0] * 150
+    for increasing in (False, True):
+        b = split_buckets(costs, 5, increasing=increasing)
+        assert b == sorted(b) and set(b) == set(range(5))            # contiguous, every bucket used
+        sizes = [b.count(k) for k in range(5)]
+        assert sizes == sorted(sizes, reverse=not increasing), sizes
+        assert abs(sizes[0] - (10 if increasing else 50)) <= 1 and abs(sizes[-1] - (50 if increasing else 10)) <= 1
+
+
 def test_zero1_pieces_partition_every_element_once():
     from triton_muon_adamw.distributed import ALIGN, shard_pieces, zero1_layout
     numels = [100, 37, 192, 5, 129, 4096, 1]
