@@ -120,6 +120,37 @@ def _worker_master(rank, world, port, q):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
 
 
+def _worker_host(rank, world, port, q):
+    """Sharded step_from_host (host gradients, copies overlapped) vs the single-GPU step()."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+        mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4, betas=(0.9, 0.95))
+        adam, muon = _params(dev)
+        sharded = MuonAdamW({"adam": adam, "muon": muon}, muon_config=mc, adam_config=ac,
+                            parameter_split="explicit", process_group=dist.group.WORLD)
+        adam1, muon1 = _params(dev)
+        single = MuonAdamW({"adam": adam1, "muon": muon1}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+        for step in range(3):
+            gs = _grads(step, dev)
+            sharded.step_from_host({p: g.cpu().pin_memory() for p, g in zip(adam + muon, gs)})
+            for p1, g in zip(adam1 + muon1, gs):
+                p1.grad = g.clone()
+            single.step()
+        torch.cuda.synchronize()
+        for p, p1 in zip(adam + muon, adam1 + muon1):
+            assert torch.equal(p.detach(), p1.detach()), f"rank {rank}: {tuple(p.shape)} differs"
+        sharded.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+
+
 def _worker(rank, world, port, q):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -201,4 +232,12 @@ def test_two_gpu_master_weights_sharded_step():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = _spawn(_worker_master, 2)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
+def test_two_gpu_step_from_host_matches_step():
+    """Host-resident gradients: each rank copies the pieces it owns, overlapped with the work."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = _spawn(_worker_host, 2)
     assert out == {0: "ok", 1: "ok"}, out

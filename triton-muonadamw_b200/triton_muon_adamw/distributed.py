@@ -506,9 +506,11 @@ class ShardedMuonAdamW:
         return dist.all_gather_into_tensor(flat, mine, group=self.pg, async_op=True)
 
     @torch.no_grad()
-    def step(self, wait_for=None):
+    def step(self, wait_for=None, adam_last=False):
         """One sharded step.  ``wait_for`` (internal): callables run before the
-        AdamW launch (index 0) and before each Muon bucket (index 1 + bucket)."""
+        AdamW launch (index 0) and before each Muon bucket (index 1 + bucket).
+        ``adam_last``: the AdamW shard after the Muon buckets instead of before
+        (the branches update disjoint parameters; results are the same)."""
         ad, mu = self.adamw, self.muon
         ad.step_num += 1
         works = []
@@ -525,12 +527,18 @@ class ShardedMuonAdamW:
             # Every rank's gradients are complete before any rank reads them, and no rank writes
             # into another's parameter replica while that rank's forward/backward may still read it.
             self._rank_sync()
-        if wait_for:
-            wait_for[0]()
-        if self.adam_shard:
-            self.backend.adamw(self._adam_quads(), lr=ad.lr, beta1=ad.beta1, beta2=ad.beta2, eps=ad.eps,
-                               weight_decay=ad.weight_decay, bias1=bias1, bias2=bias2, timer=ad._timer, reduce=red)
-            works.append(self._gather(self.adam_flat, self.adam_shard))
+
+        def adamw():
+            if wait_for:
+                wait_for[0]()
+            if self.adam_shard:
+                self.backend.adamw(self._adam_quads(), lr=ad.lr, beta1=ad.beta1, beta2=ad.beta2, eps=ad.eps,
+                                   weight_decay=ad.weight_decay, bias1=bias1, bias2=bias2, timer=ad._timer,
+                                   reduce=red)
+                works.append(self._gather(self.adam_flat, self.adam_shard))
+
+        if not adam_last:
+            adamw()
         for b, seg in enumerate(self.seg_sizes):
             if wait_for:
                 wait_for[1 + b]()
@@ -539,6 +547,8 @@ class ShardedMuonAdamW:
                               lr=mu.lr, weight_decay=mu.weight_decay, timer=mu._timer, reduce=red)
             if seg:
                 works.append(self._gather(self.muon_flats[b], seg))
+        if adam_last:
+            adamw()
         for w in works:
             w.wait()
         if red is not None or self.param_arena is not None:
@@ -550,7 +560,9 @@ class ShardedMuonAdamW:
     def step_from_host(self, host_grads):
         """:meth:`step` with gradients in host memory: each rank copies only the
         gradient pieces it reads, on a side stream, in the order the work
-        consumes them (AdamW shard, then bucket by bucket)."""
+        consumes them.  Per rank every piece takes longer to copy than to
+        update, so by Johnson's rule the Muon buckets go first, largest first,
+        and the AdamW shard (the least compute per byte) last."""
         if self.reduce_grads is not None:
             raise NotImplementedError("step_from_host takes reduced gradients; it does not combine with reduce_grads")
         main = torch.cuda.current_stream()
@@ -562,24 +574,30 @@ class ShardedMuonAdamW:
         for p in list(ad.model_params) + list(mu.model_params):
             if p.grad is None and host_grads.get(p) is not None:
                 p.grad = torch.empty_like(p)
-        events = []
+        events = [None] * (1 + len(self.seg_sizes))
+
+        def mark(k):
+            events[k] = torch.cuda.Event()
+            events[k].record(copy)
+
         with torch.cuda.stream(copy):
+            for b in range(len(self.seg_sizes)):
+                for p, s in zip(mu.model_params, self.slots):
+                    h = host_grads.get(p)
+                    if s.bucket == b and s.owner == self.rank and h is not None:
+                        p.grad.copy_(h, non_blocking=True)
+                mark(1 + b)
             for i, start, length, _ in self.adam_pieces:
                 p = ad.model_params[i]
                 h = host_grads.get(p)
                 if h is not None:
                     p.grad.reshape(-1)[start:start + length].copy_(h.reshape(-1)[start:start + length],
                                                                    non_blocking=True)
-            events.append(torch.cuda.Event())
-            events[-1].record(copy)
-            for b in range(len(self.seg_sizes)):
-                for p, s in zip(mu.model_params, self.slots):
-                    h = host_grads.get(p)
-                    if s.bucket == b and s.owner == self.rank and h is not None:
-                        p.grad.copy_(h, non_blocking=True)
-                events.append(torch.cuda.Event())
-                events[-1].record(copy)
-        self.step(wait_for=[lambda k=k: main.wait_event(events[k]) for k in range(len(events))])
+            mark(0)
+        self.step(wait_for=[lambda k=k: main.wait_event(events[k]) for k in range(len(events))], adam_last=True)
+        for p in list(ad.model_params) + list(mu.model_params):
+            if p.grad is not None:
+                p.grad.record_stream(copy)
 
     # ------------------------------------------------------------------ introspection
     def owned_muon_shapes(self):
