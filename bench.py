@@ -14,6 +14,12 @@ kernel family.  ``cpu_baseline`` times the reference's CPU path
 (``torch.optim`` AdamW(fused) + Muon, the PyTorchMuonAdamW wrapper, restated
 under oracle/) on a bounded sample and extrapolates to the full step.
 
+At N>1 the line also carries ``grad_reduce``: the step with per-rank
+(data-parallel) gradients reduced inside its first kernels (``reduce_grads``)
+against an NCCL all-reduce of the same gradient bytes (``--no-grad-reduce``
+skips it); ``--push`` picks how updated parameters reach the other ranks
+(``MuonAdamW(peer_push=...)``, default ``auto``).
+
 With ``--impl reference`` only that CPU measurement runs (rank 0), each step a
 bounded sample extrapolated to the full step.  ``--impl reference-triton``
 times the reference's own Triton ``MuonAdamW`` (the unmodified package
