@@ -195,3 +195,38 @@ def test_table_layout_constants_match_the_device_structs():
             m = re.search(r"\[(\d+)\]", n)
             off += size * (int(m.group(1)) if m else 1)
     assert off == INV_NORM_OFFSET
+
+
+def test_ctypes_structures_match_the_c_header(tmp_path):
+    """Every struct of include/muon_adamw_b200.h, compiled by gcc, has the ctypes binding's size and offsets."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    from triton_muon_adamw import _lib
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    include = Path(__file__).resolve().parent.parent / "include"
+    structs = {"mad_adamw_tensor": _lib.AdamWTensor, "mad_muon_matrix": _lib.MuonMatrix,
+               "mad_muon_plan_info": _lib.MuonPlanInfo, "mad_muon_buffers": _lib.MuonBuffers,
+               "mad_grad_reduce": _lib.GradReduce, "mad_peer_set": _lib.PeerSet}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "muon_adamw_b200.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ['printf("MAD_MAX_RANKS %d\\n", MAD_MAX_RANKS);', 'printf("MAD_IPC_HANDLE_BYTES %d\\n", MAD_IPC_HANDLE_BYTES);',
+              'printf("MAD_DTYPE_F32_MASTER %d\\n", (int)MAD_DTYPE_F32_MASTER);', "return 0; }"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", str(include), str(src), "-o", str(exe)], check=True)
+    out = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                               text=True).stdout.splitlines())
+    for cname, cls in structs.items():
+        assert int(out[f"{cname} size"]) == ctypes.sizeof(cls), cname
+        for field, _ in cls._fields_:
+            assert int(out[f"{cname} {field}"]) == getattr(cls, field).offset, (cname, field)
+    assert int(out["MAD_MAX_RANKS"]) == _lib.MAX_RANKS
+    assert int(out["MAD_IPC_HANDLE_BYTES"]) == _lib.IPC_HANDLE_BYTES
+    assert int(out["MAD_DTYPE_F32_MASTER"]) == _lib.DTYPE_F32_MASTER

@@ -151,7 +151,7 @@ def _worker_host(rank, world, port, q):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, push="auto"):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         torch.cuda.set_device(rank)
@@ -161,7 +161,7 @@ def _worker(rank, world, port, q):
         mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4, betas=(0.9, 0.95))
         adam, muon = _params(dev)
         sharded = MuonAdamW({"adam": adam, "muon": muon}, muon_config=mc, adam_config=ac,
-                            parameter_split="explicit", process_group=dist.group.WORLD)
+                            parameter_split="explicit", process_group=dist.group.WORLD, peer_push=push)
         adam1, muon1 = _params(dev)
         single = MuonAdamW({"adam": adam1, "muon": muon1}, muon_config=mc, adam_config=ac, parameter_split="explicit")
         for step in range(3):
@@ -211,10 +211,12 @@ def _spawn(target, world, *extra):
     return out
 
 
-def test_two_gpu_sharded_step_is_bit_identical():
+@pytest.mark.parametrize("push", ["auto", "nccl", "kernel", "hybrid"])
+def test_two_gpu_sharded_step_is_bit_identical(push):
+    """Every way of exchanging the updated parameters (peer_push) gives the single-GPU result."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    out = _spawn(_worker, 2)
+    out = _spawn(_worker, 2, push)
     assert out == {0: "ok", 1: "ok"}, out
 
 
