@@ -240,11 +240,48 @@ def _worker(rank, world, port, mode, q):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-800:]}"))
 
 
-def _run(world, mode):
+def _worker_edge(rank, world, port, case, q):
+    """Degenerate layouts: a branch without parameters, more ranks and buckets than Muon matrices."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+        from triton_muon_adamw import AdamConfig, MuonConfig
+        from triton_muon_adamw.distributed import ShardedMuonAdamW
+        adam, muon = _make()
+        if case == "no_adam":
+            adam = []
+        elif case == "no_muon":
+            muon = []
+        elif case == "few_muon":
+            muon = muon[:2]
+        ref = OracleMuonAdamW([p.detach().clone() for p in adam], [p.detach().clone() for p in muon],
+                              adam=ADAM, muon=MUON)
+        opt = ShardedMuonAdamW(adam, muon, MuonConfig(**MUON), AdamConfig(**ADAM), dist.group.WORLD, n_buckets=5,
+                               backend=OracleBackend())
+        for step in range(2):
+            ga, gm = _grads(step)
+            ga, gm = ga[:len(adam)], [g for g, _ in zip(gm, muon)]
+            for p, g in zip(adam + muon, ga + gm):
+                p.grad = g.clone()
+            opt.step()
+            ref.step(ga, gm)
+        for p, r in zip(adam + muon, ref.params_adam + ref.params_muon):
+            assert torch.equal(p.detach(), r), f"rank {rank}: {case} parameter {tuple(p.shape)} differs"
+        sd = opt.state_dict()
+        assert len(sd["adam"]["state"]) == len(adam) and len(sd["muon"]["state"]) == len(muon)
+        opt.load_state_dict(sd)
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-800:]}"))
+
+
+def _run(world, mode, target=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    procs = [ctx.Process(target=target or _worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -269,6 +306,12 @@ def test_sharded_step_bf16_parameters():
     """bf16 parameters: bf16 flat buffers and momentum, float32 AdamW moment shards."""
     out = _run(2, "bf16")
     assert out == {0: "ok", 1: "ok"}, out
+
+
+@pytest.mark.parametrize("world,case", [(2, "no_adam"), (2, "no_muon"), (3, "few_muon")])
+def test_sharded_step_degenerate_layouts(world, case):
+    out = _run(world, case, target=_worker_edge)
+    assert out == {r: "ok" for r in range(world)}, out
 
 
 def test_sharded_step_master_weights():
