@@ -9,7 +9,6 @@ single-process oracle run.
 
 from __future__ import annotations
 
-import math
 import os
 import socket
 import traceback
