@@ -230,3 +230,19 @@ def test_ctypes_structures_match_the_c_header(tmp_path):
     assert int(out["MAD_MAX_RANKS"]) == _lib.MAX_RANKS
     assert int(out["MAD_IPC_HANDLE_BYTES"]) == _lib.IPC_HANDLE_BYTES
     assert int(out["MAD_DTYPE_F32_MASTER"]) == _lib.DTYPE_F32_MASTER
+
+
+def test_muonadamw_rejects_bad_options_before_touching_the_gpu():
+    """Argument errors surface at construction, on any device (construction makes no CUDA call)."""
+    from triton_muon_adamw import MuonAdamW
+    params = {"adam": [nn.Parameter(torch.zeros(4))], "muon": [nn.Parameter(torch.zeros(4, 4))]}
+    with pytest.raises(ValueError):
+        MuonAdamW(params, parameter_split="explicit", peer_push="bogus")
+    with pytest.raises(ValueError):
+        MuonAdamW(params, parameter_split="explicit", reduce_grads="max")
+    with pytest.raises(TypeError):
+        MuonAdamW(params, parameter_split="explicit", master_weights=True)     # float32 parameters
+    opt = MuonAdamW({k: [nn.Parameter(p.detach().to(torch.bfloat16)) for p in v] for k, v in params.items()},
+                    parameter_split="explicit", master_weights=True)
+    assert all(m.dtype == torch.float32 for m in opt.muon.masters.values())
+    assert all(m.dtype == torch.float32 for m in opt.muon.momentum.values())

@@ -186,6 +186,9 @@ class MuonAdamW(TritonMuon, TritonAdamW):
     ) -> None:
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
+        from .distributed import CudaBackend  # noqa: PLC0415
+        if peer_push not in CudaBackend.PUSH_MODES:
+            raise ValueError(f"peer_push must be one of {CudaBackend.PUSH_MODES}, got {peer_push!r}")
         adam_params, muon_params = split_parameters(model_params, parameter_split)
         self.master_weights = bool(master_weights)
         if self.master_weights and any(p.dtype != torch.bfloat16 for p in adam_params + muon_params):
@@ -193,7 +196,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         self.process_group = process_group
         self.distributed = None
         if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
-            from .distributed import CudaBackend, ShardedMuonAdamW  # noqa: PLC0415
+            from .distributed import ShardedMuonAdamW  # noqa: PLC0415
             self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group,
                                                 reduce_grads=reduce_grads, backend=CudaBackend(push=peer_push),
                                                 master_weights=self.master_weights)
