@@ -249,6 +249,10 @@ def main():
                     help="at N>1, how updated parameters reach the other ranks (MuonAdamW peer_push)")
     ap.add_argument("--no-grad-reduce", action="store_true",
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="at N=1, skip timing the reference's own Triton MuonAdamW on this GPU after our arm")
+    ap.add_argument("--no-verify", action="store_true",
+                    help="at N>1, skip the post-timing check of every replica against a single-GPU recomputation")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
 
@@ -373,6 +377,12 @@ def main():
                 "ns_ms_per_step": round(ns_ms, 3), "ns_flops_per_step": ns_total}
     launches_per_step = sum(len(v) for v in per.values()) / timing_steps
 
+    # At N>1: one more (untimed) step, checked -- replicas bit-identical on every rank, and rank 0
+    # recomputes matrices and AdamW tensors owned by other ranks with the single-GPU optimizer.
+    parity = None
+    if world > 1 and not args.no_verify:
+        parity = verify_sharded_step(opt, rank, world, barrier)
+
     # End to end: this step's gradients from pinned host memory, result read back.
     e2e = run_e2e(opt, model, dev, args, barrier, world)
 
@@ -386,13 +396,26 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, cores, detail = cpu_sample(args.config, cfg["adam"], args.ns_steps)
         cpu = {"value": round(v, 1), "unit": "ms/step", "cores": cores, "kind": "port", "sample": sample,
-               "per_shape_ms": detail}
+               "per_shape_ms": detail, "extrapolated": True}
+
+    # The reference's own Triton MuonAdamW on this GPU, same config, in a child process once our
+    # state is freed (both do not fit in HBM together at 8B).
+    ref_triton = None
+    if world == 1 and not args.no_reference_triton:
+        import gc  # noqa: PLC0415
+        opt_branch_timer(opt, None)
+        del opt, model
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        ref_triton = run_reference_triton_child(args)
 
     if rank == 0:
         line = {
             "metric": f"MuonAdamW ms/step ({cfg['name']})", "value": round(ms, 3), "unit": "ms/step",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32 params/grads/moments/momentum (elementwise fp32); Newton-Schulz bf16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) params, N(0,1e-3) grads; no dataset)",
             "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "muon_matrices": n_muon,
                        "adamw_tensors": n_adam, "ns_steps": args.ns_steps, "coeffs": list(COEFFS),
@@ -405,7 +428,23 @@ def main():
         }
         if grad_reduce is not None:
             line["grad_reduce"] = grad_reduce
+        if parity is not None:
+            line["parity"] = parity["status"]
+            line["parity_detail"] = parity
+        if ref_triton is not None:
+            line["reference_triton"] = ref_triton
+            rv = ref_triton.get("value")
+            if rv:
+                line["vs_reference_triton"] = round(rv / ms, 3)
+                ours_mhz, ref_mhz = clock_info.get("sm_mhz"), (ref_triton.get("clocks") or {}).get("sm_mhz")
+                if ours_mhz and ref_mhz:
+                    # cycles per step, ours vs the reference's: the ratio with each arm's own SM clock taken out
+                    line["vs_reference_triton_per_clock"] = round(rv * ref_mhz / (ms * ours_mhz), 3)
         print(json.dumps(line), flush=True)
+    if parity is not None and parity["status"] != "ok":
+        if world > 1:
+            dist.destroy_process_group()
+        sys.exit(1)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -540,14 +579,161 @@ def run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier):
                     "gradients needs first; compare fused_step_ms with nccl_allreduce_ms + value"}
 
 
+@torch.no_grad()
+def verify_sharded_step(opt, rank, world, barrier):
+    """One more sharded step, checked (N>1; collective).
+
+    * Replicas: a bit-exact checksum (int64 sum of each parameter's raw bits)
+      of every parameter on every rank; all ranks must agree.
+    * Recomputation: rank 0 snapshots up to three Muon matrices owned by other
+      ranks (momentum sent by the owner) and two AdamW tensors (moments
+      gathered from the ZeRO-1 shards), steps them with the single-GPU
+      ``TritonMuon`` / ``TritonAdamW`` on the same gradients, and requires the
+      result to equal its replica bit for bit: the sharded step is the
+      single-GPU step, whatever rank owns a matrix or a range.
+    """
+    from triton_muon_adamw.adamw import TritonAdamW  # noqa: PLC0415
+    from triton_muon_adamw.muon import TritonMuon  # noqa: PLC0415
+    sh = opt.distributed
+    mu, ad = sh.muon, sh.adamw
+    # Muon matrices owned elsewhere, one per distinct shape, owners spread out.
+    picks, seen = [], set()
+    for i, s in enumerate(sh.slots):
+        shape = tuple(mu.model_params[i].shape)
+        if s.owner != 0 and shape not in seen and mu.model_params[i].grad is not None:
+            picks.append(i)
+            seen.add(shape)
+        if len(picks) == 3:
+            break
+    snaps = []
+    for i in picks:
+        p, s = mu.model_params[i], sh.slots[i]
+        mom = mu.momentum[p].clone() if s.owner == rank else torch.empty_like(p, dtype=sh.mom_segs[0].dtype)
+        dist.broadcast(mom, src=s.owner, group=sh.pg)
+        if rank == 0:
+            snaps.append((i, p.detach().clone(), mom, p.grad.clone()))
+        else:
+            del mom
+    adam_picks = [0, len(ad.model_params) - 1] if ad.model_params else []
+    full_m = torch.empty(sh.adam_shard * world, dtype=torch.float32, device=sh.device)
+    full_v = torch.empty_like(full_m)
+    dist.all_gather_into_tensor(full_m, sh.exp_avg, group=sh.pg)
+    dist.all_gather_into_tensor(full_v, sh.exp_avg_sq, group=sh.pg)
+    adam_snaps = []
+    if rank == 0:
+        for i in adam_picks:
+            p, o, n = ad.model_params[i], sh.adam_offsets[i], sh.adam_numels[i]
+            adam_snaps.append((i, p.detach().clone(), full_m[o:o + n].view_as(p).clone(),
+                               full_v[o:o + n].view_as(p).clone(), p.grad.clone()))
+    del full_m, full_v
+    step_before = ad.step_num
+    barrier()
+    opt.step()
+    barrier()
+
+    def bits(t):
+        raw = t.detach().reshape(-1)
+        raw = raw.view(torch.int32) if raw.element_size() == 4 else raw.view(torch.int16)
+        return raw.to(torch.int64).sum()
+
+    params = list(ad.model_params) + list(mu.model_params)
+    sums = torch.stack([bits(p) for p in params])
+    every = [torch.empty_like(sums) for _ in range(world)]
+    dist.all_gather(every, sums, group=sh.pg)
+    mismatched = [r for r in range(world) if not torch.equal(every[r], every[0])]
+    out = {"replicas_identical": not mismatched, "ranks_checked": world, "params_checked": len(params),
+           "muon_recomputed": [], "adamw_recomputed": []}
+    problems = [f"replica of rank {r} differs from rank 0" for r in mismatched]
+    if rank == 0:
+        for i, p0, mom, g in snaps:
+            p = mu.model_params[i]
+            q = torch.nn.Parameter(p0)
+            single = TritonMuon([q], lr=mu.lr, weight_decay=mu.weight_decay, coeffs=(mu.a, mu.b, mu.c),
+                                nesterov=mu.is_nesterov, beta=mu.beta, ns_steps=mu.steps, eps=mu.eps,
+                                adjust_lr_fn=mu.adjust_lr_fn)
+            single.momentum[q].copy_(mom)
+            q.grad = g
+            single.step()
+            ok = torch.equal(q.detach(), p.detach())
+            out["muon_recomputed"].append({"index": i, "shape": list(p.shape), "owner": sh.slots[i].owner,
+                                           "bit_equal": ok})
+            if not ok:
+                problems.append(f"Muon matrix {i} {tuple(p.shape)} (owner {sh.slots[i].owner}) differs")
+        for i, p0, m, v, g in adam_snaps:
+            p = ad.model_params[i]
+            q = torch.nn.Parameter(p0)
+            single = TritonAdamW([q], lr=ad.lr, betas=(ad.beta1, ad.beta2), weight_decay=ad.weight_decay, eps=ad.eps)
+            single.m[q].copy_(m)
+            single.v[q].copy_(v)
+            single.step_num = step_before
+            q.grad = g
+            single.step()
+            ok = torch.equal(q.detach(), p.detach())
+            out["adamw_recomputed"].append({"index": i, "numel": p.numel(), "bit_equal": ok})
+            if not ok:
+                problems.append(f"AdamW tensor {i} ({p.numel()} elements) differs")
+        torch.cuda.synchronize()
+    status = "ok" if not problems else "FAIL: " + "; ".join(problems)
+    flag = torch.tensor([0 if status == "ok" else 1], device=sh.device)
+    dist.all_reduce(flag, group=sh.pg)
+    out["status"] = "ok" if int(flag.item()) == 0 else (status if status != "ok" else "FAIL on another rank")
+    return out
+
+
+def run_reference_triton_child(args):
+    """``bench.py --impl reference-triton`` as a child process; its JSON line (or why it is missing)."""
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT")}
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference-triton", "--steps", str(args.steps),
+           "--warmup", str(args.warmup), "--config", args.config, "--ns-steps", str(args.ns_steps)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=1800)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference-triton child run exceeded 1800 s"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            d = json.loads(line)
+            keep = ("value", "unit", "steps", "warmup", "clocks", "unavailable", "config")
+            return {k: d[k] for k in keep if k in d}
+    return {"unavailable": f"reference-triton child exited {r.returncode}: {r.stderr.strip()[-300:]}"}
+
+
 def e2e_grad_tensors(opt, model):
     if getattr(opt, "distributed", None) is not None:
         return opt.distributed.local_grad_tensors()
     return [p.grad for p in model.parameters() if p.grad is not None]
 
 
+def c1_cpu_direct(steps=10):
+    """The C1 config (17M GPT, tied embedding) through the reference wrapper's CPU path, timed directly."""
+    from oracle.muon_adamw_oracle import ReferenceWrapperCPU, gpt_c1_shapes  # noqa: PLC0415
+    adam_shapes, muon_shapes = gpt_c1_shapes()
+    gen = torch.Generator().manual_seed(0)
+    adam = [nn.Parameter(torch.randn(s, generator=gen) * 0.02) for s in adam_shapes]
+    muon = [nn.Parameter(torch.randn(s, generator=gen) * 0.02) for s in muon_shapes]
+    for p in adam + muon:
+        p.grad = torch.randn(p.shape, generator=gen) * 1e-3
+    w = ReferenceWrapperCPU(adam, muon, adam=dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-7, weight_decay=0.01),
+                            muon=dict(lr=1e-3, beta=0.95, eps=1e-7, weight_decay=0.1, nesterov=True, ns_steps=5,
+                                      adjust_lr_fn="original"))
+    w.step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        w.step()
+    return {"value": round((time.perf_counter() - t0) * 1e3 / steps, 2), "unit": "ms/step", "steps": steps,
+            "params": sum(p.numel() for p in adam + muon),
+            "what": "C1 (17M GPT, d=512, 4 layers, vocab 8192 tied) through the wrapper's CPU path, timed "
+                    "directly, not extrapolated"}
+
+
 def run_reference_arm(args, cfg, world):
-    """The reference's CPU path on the host cores, bounded sample per step, extrapolated."""
+    """The reference's CPU path on the host cores, bounded sample per step, extrapolated.
+
+    Each of the K "steps" is one sampled round: one matrix per distinct Muon
+    shape and one AdamW chunk, timed and scaled by the shape counts -- the
+    8B step does not fit in host memory.  The line says so (``extrapolated``,
+    ``sampled_rounds``) and adds C1 timed directly as a cross-check.
+    """
     vals, sample, cores = [], "", 1
     for i in range(args.warmup + args.steps):
         v, sample, cores, _ = cpu_sample(args.config, cfg["adam"], args.ns_steps)
@@ -556,12 +742,14 @@ def run_reference_arm(args, cfg, world):
     ms = statistics.mean(vals)
     line = {"metric": f"MuonAdamW ms/step ({cfg['name']})", "value": round(ms, 1), "unit": "ms/step",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1),
-            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "impl": "reference",
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32 params/state; Newton-Schulz bf16 (torch CPU)", "data": "synthetic", "impl": "reference",
+            "extrapolated": True, "sampled_rounds": args.steps,
             "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "ns_steps": args.ns_steps,
                        "parallelism": "host cores"},
             "cpu_baseline": {"value": round(ms, 1), "unit": "ms/step", "cores": cores, "kind": "port",
-                             "sample": sample},
+                             "sample": sample, "extrapolated": True},
+            "c1_direct": c1_cpu_direct(),
             "e2e": {"value": round(ms, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

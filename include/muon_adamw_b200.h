@@ -213,7 +213,10 @@ int mad_muon_step_multi_reduce(const mad_muon_plan_info* info, void* dev_table, 
  * mad_muon_plan and calling mad_muon_step_multi; lr_scale as in
  * mad_muon_matrix.  The first call on a device resolves the array's address
  * for that device, so make it before any stream capture.  Each call uploads
- * its plan synchronously; calls that overlap on the GPU race on the array. */
+ * its plan synchronously and, once its kernels have finished, reads their
+ * status word back: MAD_ERR_DEVICE if one gave up waiting on a barrier (the
+ * parameter and momentum it wrote are then invalid).  Calls that overlap on
+ * the GPU race on the array. */
 int mad_muon_step_noalloc(float* param, const float* grad, float* momentum, int64_t rows, int64_t cols,
                           double lr_scale, double beta, int32_t nesterov, float a, float b, float c, int32_t ns_steps,
                           float eps, double lr, double weight_decay, void* stream);
@@ -259,6 +262,14 @@ int mad_peer_push(const void* src, int64_t bytes, const mad_peer_set* peers, voi
  * waiting on a barrier; the step's results are then invalid. */
 int mad_muon_read_status(const mad_muon_plan_info* info, void* dev_table, uint32_t* status, int32_t clear,
                          void* stream);
+
+/* Test hook (no counterpart in the reference): the next n_launches
+ * Newton-Schulz Gram launches of this process run with an idle TMA producer
+ * and a ~10 ms barrier-wait limit, so their waits expire with no copy or MMA
+ * in flight.  Lets a test drive the kernels' error path -- status bits
+ * DEV_ERR_MBAR_TIMEOUT_MMA and _EPILOGUE, MAD_ERR_DEVICE from
+ * mad_muon_step_noalloc -- without faulting or hanging the GPU.  0 disarms. */
+int mad_debug_expire_next_waits(int32_t n_launches);
 
 #ifdef __cplusplus
 }

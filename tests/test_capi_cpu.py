@@ -246,3 +246,34 @@ def test_muonadamw_rejects_bad_options_before_touching_the_gpu():
                     parameter_split="explicit", master_weights=True)
     assert all(m.dtype == torch.float32 for m in opt.muon.masters.values())
     assert all(m.dtype == torch.float32 for m in opt.muon.momentum.values())
+
+
+@pytest.mark.parametrize("bad_delta", [8, 4, -24, 1])
+def test_gradient_reduction_rejects_unaligned_peer_deltas_before_any_launch(bad_delta):
+    """Peer copies are read with 16-byte vector loads at g + delta[k]: a delta off that grid is refused."""
+    from triton_muon_adamw import _lib
+    lib = _lib.load()
+    red = _lib.GradReduce(2, 0.5)
+    red.delta[0], red.delta[1] = 0, 1 << 20
+    red.delta[1] += bad_delta
+    fake_table = ctypes.c_void_p(0x10000)      # never dereferenced: the check fails first
+    rc = lib.mad_adamw_step_multi_reduce(fake_table, 1, 1e-3, 0.9, 0.999, 1e-8, 0.01, 0.1, 0.1,
+                                         ctypes.byref(red), None)
+    assert rc == 2 and b"not a multiple of 16" in lib.mad_last_error()
+    info = _lib.MuonPlanInfo()
+    info.n_mats = 1
+    rc = lib.mad_muon_prep_reduce(ctypes.byref(info), fake_table, 0.95, 1, 1e-7, ctypes.byref(red), None)
+    assert rc == 2 and b"not a multiple of 16" in lib.mad_last_error()
+    rc = lib.mad_muon_step_multi_reduce(ctypes.byref(info), fake_table, 0.95, 1, 3.4, -4.7, 2.0, 5, 1e-7, 1e-3,
+                                        0.1, ctypes.byref(red), None)
+    assert rc == 2 and b"not a multiple of 16" in lib.mad_last_error()
+
+
+def test_reference_install_is_importable_beside_ours():
+    """The unmodified reference under baseline/_ref loads under its alias without shadowing our package."""
+    import triton_muon_adamw as ours
+    from reference_pkg import load_reference
+    R = load_reference()
+    assert R.__name__ == "ref_triton_muon_adamw" and R.MuonAdamW is not ours.MuonAdamW
+    assert "baseline" in R.__file__ and "baseline" not in ours.__file__
+    assert hasattr(R.muon.triton_muon, "TritonMuon") and hasattr(R, "PyTorchMuonAdamW")

@@ -231,6 +231,29 @@ def _worker(rank, world, port, mode, q):
         sd2 = opt.state_dict()
         assert torch.equal(sd2["adam"]["state"][0]["exp_avg"], sd["adam"]["state"][0]["exp_avg"])
         assert torch.equal(sd2["muon"]["state"][3]["momentum_buffer"], sd["muon"]["state"][3]["momentum_buffer"])
+        if master:
+            # A dict without masters (PyTorchMuonAdamW's layout) after the model's parameters changed: the
+            # masters restart from the current bf16 parameters, and the next step continues from them.
+            with torch.no_grad():
+                for p in adam + muon:
+                    p.mul_(0.5)
+            bare = {k: {"state": {i: {n: t for n, t in st.items() if n != "master_param"}
+                                  for i, st in sd[k]["state"].items()},
+                        "param_groups": sd[k]["param_groups"]} for k in ("adam", "muon")}
+            opt.load_state_dict(bare)
+            sd3 = opt.state_dict()
+            for k, ps in (("adam", adam), ("muon", muon)):
+                for i, p in enumerate(ps):
+                    assert torch.equal(sd3[k]["state"][i]["master_param"], p.detach().float()), (k, i)
+            for r, p in zip(ref.params_adam + ref.params_muon, adam + muon):
+                r.copy_(p.detach().float())
+            ga, gm = _grads(2, dtype)
+            for p, g in zip(adam + muon, ga + gm):
+                p.grad = g.clone()
+            opt.step()
+            ref.step([g.float() for g in ga], [g.float() for g in gm])
+            for p, r in zip(adam + muon, ref.params_adam + ref.params_muon):
+                assert torch.equal(p.detach(), r.to(dtype)), f"rank {rank}: {tuple(p.shape)} after a master-less load"
         dist.destroy_process_group()
         q.put((rank, "ok"))
     except SystemExit:

@@ -47,6 +47,12 @@ inline int grad_reduce_from(const mad_grad_reduce* in, GradReduce* out, const ch
   if (in->n_ranks < 1 || in->n_ranks > MAX_RANKS)
     return fail(MAD_ERR_INVALID, "%s: n_ranks %d outside 1..%d", who, in->n_ranks, MAX_RANKS);
   if (!std::isfinite(in->scale)) return fail(MAD_ERR_INVALID, "%s: non-finite gradient scale", who);
+  // The kernels read every rank's copy with 16-byte vector loads at g + delta[k];
+  // a delta off that grid would make those loads misaligned on the device.
+  for (int k = 0; k < in->n_ranks; ++k)
+    if (in->delta[k] % 16 != 0)
+      return fail(MAD_ERR_ALIGN, "%s: delta[%d] = %lld is not a multiple of 16 bytes", who, k,
+                  static_cast<long long>(in->delta[k]));
   out->n = in->n_ranks;
   out->scale = in->scale;
   for (int k = 0; k < in->n_ranks; ++k) out->delta[k] = in->delta[k];

@@ -19,7 +19,10 @@
 // without ordering) race on it.  The first call on a device resolves the
 // array's device address for that device (cudaGetSymbolAddress), so make the
 // first call before any stream capture.  Each call uploads its plan with a
-// synchronous copy, which also waits for the stream's earlier work.
+// synchronous copy, which also waits for the stream's earlier work, and after
+// its kernels reads their status word back (waiting for them to finish): a
+// kernel that gave up waiting on a barrier makes the call return
+// MAD_ERR_DEVICE.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -198,5 +201,16 @@ extern "C" int mad_muon_step_noalloc(float* param, const float* grad, float* mom
           cudaSuccess ||
       cudaStreamSynchronize(s) != cudaSuccess)
     return fail_cuda("mad_muon_step_noalloc: plan upload");
-  return mad_muon_step_multi(&info, table, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay, stream);
+  if (int rc = mad_muon_step_multi(&info, table, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay, stream))
+    return rc;
+  // The caller holds no plan to read the kernels' status word from, and the
+  // next call rewrites it: read it here, after this call's kernels finish.
+  uint32_t status = 0;
+  if (int rc = mad_muon_read_status(&info, table, &status, 1, stream)) return rc;
+  if (status != 0)
+    return fail(MAD_ERR_DEVICE,
+                "mad_muon_step_noalloc: a Newton-Schulz kernel gave up waiting on a barrier (status 0x%x); the "
+                "parameter and momentum written by this call are invalid",
+                status);
+  return MAD_OK;
 }

@@ -29,6 +29,8 @@
 // the K index).
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "capi_common.h"
 #include "elem_io.cuh"
 #include "plan.cuh"
@@ -71,6 +73,8 @@ struct GemmArgs {
   float lr_wd;
   double lr;
   unsigned int* status;
+  long long wait_limit;  // SM cycles before a barrier wait gives up
+  int idle_producer;     // test launches only: the producer issues no loads, so the waits expire
 };
 
 __device__ __forceinline__ int k_extent(int mode, const MatDesc& md) { return mode == GRAM ? md.n : md.m; }
@@ -87,7 +91,7 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
   uint32_t phase = 0;
   const int cur = args.iter & 1;
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-  bool ok = true;
+  bool ok = !args.idle_producer;
   for (int t = cid; t < args.n_tiles && ok; t += ncl) {
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
@@ -108,7 +112,8 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
     const int bcol = tr.tn * BN + static_cast<int>(rank) * (BN / 2);   // this CTA's B columns
     const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
     for (int kb = 0; kb < nkb; ++kb) {
-      if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_PRODUCER) || *abort_flag) {
+      if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_PRODUCER, args.wait_limit) ||
+          *abort_flag) {
         *abort_flag = 1;
         ok = false;
         break;
@@ -150,14 +155,15 @@ __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, ui
     const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
     const int acc = lt & 1;
     const uint32_t acc_phase = static_cast<uint32_t>((lt >> 1) & 1);
-    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_MMA) || *abort_flag) {
+    if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_MMA, args.wait_limit) ||
+        *abort_flag) {
       *abort_flag = 1;
       break;
     }
     tc_fence_after();
     const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
     for (int kb = 0; kb < nkb; ++kb) {
-      if (!mbar_wait(&full[stage], phase, args.status, DEV_ERR_MBAR_TIMEOUT_MMA) || *abort_flag) {
+      if (!mbar_wait(&full[stage], phase, args.status, DEV_ERR_MBAR_TIMEOUT_MMA, args.wait_limit) || *abort_flag) {
         *abort_flag = 1;
         ok = false;
         break;
@@ -465,7 +471,8 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     } else if (nch > 0 && row_ok) {
       chunk_prefetch<MODE>(args, md, grow, col0, in[0]);
     }
-    if (!mbar_wait(&tfull[acc_buf], acc_phase, args.status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE) || *abort_flag) {
+    if (!mbar_wait(&tfull[acc_buf], acc_phase, args.status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE, args.wait_limit) ||
+        *abort_flag) {
       *abort_flag = 1;
       break;
     }
@@ -598,6 +605,12 @@ static int launch(const GemmArgs& args, cudaStream_t stream, const char* name) {
   return check_launch(name);
 }
 
+// Gram launches still to run with an idle producer and a short wait limit
+// (mad_debug_expire_next_waits).  The Gram epilogue reads no input and the idle
+// producer issues no load, so when the waits of such a launch expire nothing
+// is in flight: the error path runs without any risk to the GPU.
+std::atomic<int> g_expire_gram_launches{0};
+
 }  // namespace ns
 
 int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, const TileRef* tiles, int64_t n_tiles,
@@ -615,6 +628,13 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
   args.lr_wd = lr_wd;
   args.lr = lr;
   args.status = status;
+  args.wait_limit = MBAR_WAIT_LIMIT_CYCLES;
+  args.idle_producer = 0;
+  if (mode == ns::GRAM && ns::g_expire_gram_launches.load(std::memory_order_relaxed) > 0 &&
+      ns::g_expire_gram_launches.fetch_sub(1) > 0) {
+    args.wait_limit = MBAR_WAIT_LIMIT_TEST_CYCLES;
+    args.idle_producer = 1;
+  }
   switch (mode) {
     case ns::GRAM:
       return ns::launch<ns::GRAM>(args, stream, "ns_gemm_kernel<GRAM>");
@@ -627,3 +647,12 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
 }
 
 }  // namespace mad
+
+// Arms the next n_launches Newton-Schulz Gram launches of this process so that
+// their barrier waits expire (see g_expire_gram_launches).
+extern "C" int mad_debug_expire_next_waits(int32_t n_launches) {
+  mad::clear_error();
+  if (n_launches < 0) return mad::fail(MAD_ERR_INVALID, "mad_debug_expire_next_waits: negative count");
+  mad::ns::g_expire_gram_launches.store(n_launches);
+  return MAD_OK;
+}

@@ -13,6 +13,8 @@
 namespace mad {
 
 constexpr long long MBAR_WAIT_LIMIT_CYCLES = 4000000000LL;
+// Limit of a launch armed by mad_debug_expire_next_waits (about 10 ms).
+constexpr long long MBAR_WAIT_LIMIT_TEST_CYCLES = 20000000LL;
 
 // Error bits a kernel may set in its status word (read back by the host).
 enum : unsigned int {
@@ -57,15 +59,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and
-// sets `err_bit` in *err) if it did not within the cycle limit.
+// sets `err_bit` in *err) if it did not within `limit` SM cycles.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err,
-                                          unsigned int err_bit) {
+                                          unsigned int err_bit, long long limit = MBAR_WAIT_LIMIT_CYCLES) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
-    if (clock64() - t0 > MBAR_WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       atomicOr(err, err_bit);
       return false;
     }

@@ -14,6 +14,9 @@ from pathlib import Path
 LIB_NAME = "libmuonadamw_b200.so"
 ABI_VERSION = 4  # mad_abi_version() of the library these structures describe
 DTYPE_F32, DTYPE_BF16, DTYPE_F32_MASTER = 0, 1, 2  # MAD_DTYPE_*
+ERR_DEVICE = 5            # MAD_ERR_DEVICE: a kernel reported an error in its status word
+# Status bits of the Muon kernels (a barrier wait that gave up, by role).
+DEV_ERR_TIMEOUT_PRODUCER, DEV_ERR_TIMEOUT_MMA, DEV_ERR_TIMEOUT_EPILOGUE, DEV_ERR_TIMEOUT_DRAIN = 1, 2, 4, 8
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 c_int32 = ctypes.c_int32
@@ -99,6 +102,7 @@ SIGNATURES = {
     "mad_ipc_close": (ctypes.c_int, [c_void_p]),
     "mad_copy_async": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "mad_peer_push": (ctypes.c_int, [c_void_p, c_int64, ctypes.POINTER(PeerSet), c_void_p]),
+    "mad_debug_expire_next_waits": (ctypes.c_int, [c_int32]),
 }
 
 _lib = None

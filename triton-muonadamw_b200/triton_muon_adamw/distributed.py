@@ -675,8 +675,11 @@ class ShardedMuonAdamW:
                     continue
                 self.exp_avg[sh:sh + length].copy_(st["exp_avg"].reshape(-1)[start:start + length])
                 self.exp_avg_sq[sh:sh + length].copy_(st["exp_avg_sq"].reshape(-1)[start:start + length])
-                if self.master_weights and "master_param" in st:
-                    self.adam_master[sh:sh + length].copy_(st["master_param"].reshape(-1)[start:start + length])
+                if self.master_weights:
+                    # A dict without masters (PyTorchMuonAdamW's, or a checkpoint saved without them): the
+                    # masters restart from the current bf16 parameters, as the single-GPU path does.
+                    src = st["master_param"] if "master_param" in st else ad.model_params[i].detach()
+                    self.adam_master[sh:sh + length].copy_(src.reshape(-1)[start:start + length])
             for st in a["state"].values():
                 steps.append(int(float(st["step"])))
             ad.step_num = max(steps) if steps else 0
@@ -689,12 +692,15 @@ class ShardedMuonAdamW:
             mu.eps, mu.steps = g.get("eps", mu.eps), g.get("ns_steps", mu.steps)
             mu.adjust_lr_fn = g.get("adjust_lr_fn") or "original"
             for i, (p, s) in enumerate(zip(mu.model_params, self.slots)):
+                if p not in mu.momentum:        # owned by another rank
+                    continue
                 st = m["state"].get(i)
-                if st is not None and p in mu.momentum:
+                if st is not None and "momentum_buffer" in st:
                     mu.momentum[p].copy_(st["momentum_buffer"])
-                    if self.master_weights and "master_param" in st:
-                        o = s.offset - self.rank * self.seg_sizes[s.bucket]
-                        self.master_segs[s.bucket][o:o + s.numel].copy_(st["master_param"].reshape(-1))
+                if self.master_weights:
+                    src = st["master_param"] if st is not None and "master_param" in st else p.detach()
+                    o = s.offset - self.rank * self.seg_sizes[s.bucket]
+                    self.master_segs[s.bucket][o:o + s.numel].copy_(src.reshape(-1))
 
 
 __all__ = ["ShardedMuonAdamW", "CudaBackend", "lpt_assign", "split_buckets", "muon_layout", "zero1_layout",
