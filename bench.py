@@ -251,6 +251,9 @@ def main():
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="at N=1, skip timing the reference's own Triton MuonAdamW on this GPU after our arm")
+    ap.add_argument("--realloc-grads", action="store_true",
+                    help="alternate every step between two sets of gradient tensors (new .grad addresses each "
+                         "step, as zero_grad(set_to_none=True) + backward gives): the plans patch the addresses")
     ap.add_argument("--no-verify", action="store_true",
                     help="at N>1, skip the post-timing check of every replica against a single-GPU recomputation")
     args = ap.parse_args()
@@ -299,8 +302,19 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
+    step_params = [p for p in model.parameters() if p.grad is not None]
+    grad_sets = None
+    if args.realloc_grads:
+        grad_sets = [[p.grad for p in step_params], [p.grad.clone() for p in step_params]]
+
+    def timed_step(i):
+        if grad_sets is not None:
+            for p, g in zip(step_params, grad_sets[i % 2]):
+                p.grad = g
         opt.step()
+
+    for i in range(args.warmup):
+        timed_step(i)
     barrier()
 
     clocks = ClockSampler(local_rank)
@@ -308,8 +322,8 @@ def main():
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     start.record()
-    for _ in range(args.steps):
-        opt.step()
+    for i in range(args.steps):
+        timed_step(i)
     end.record()
     barrier()
     clock_info = clocks.stop()
@@ -320,6 +334,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
+    if grad_sets is not None:
+        for p, g in zip(step_params, grad_sets[0]):
+            p.grad = g
+        grad_sets = None
     # Per-kernel timing: one more pass with CUDA events between every launch.
     timer = PhaseTimer()
     opt_branch_timer(opt, timer)
@@ -420,7 +438,7 @@ def main():
             "config": {"workload": f"{cfg['name']} MuonAdamW optimizer step", "muon_matrices": n_muon,
                        "adamw_tensors": n_adam, "ns_steps": args.ns_steps, "coeffs": list(COEFFS),
                        "parallelism": "single-gpu" if world == 1 else f"muon-owner+zero1-adamw x{world}",
-                       "param_push": push_mode,
+                       "param_push": push_mode, "realloc_grads": bool(args.realloc_grads),
                        "l2": "inputs (fp32 grads/params/momentum, > 100 GB) exceed L2; no flush needed",
                        "elementwise_dtype": "fp32"},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": int(round(launches_per_step * args.steps)),

@@ -105,6 +105,14 @@ int mad_adamw_table_bytes(const mad_adamw_tensor* tensors, int32_t n_tensors, in
 int mad_adamw_plan(const mad_adamw_tensor* tensors, int32_t n_tensors, void* dev_table, int64_t table_bytes,
                    int64_t* n_tiles, void* stream);
 
+/* Replaces the gradient address of every planned tensor (grads[i] for the
+ * tensor planned i-th) without re-planning: one small kernel on `stream`,
+ * ordered after the work already queued there, no synchronisation.  For
+ * gradients re-allocated between steps (the reference reads p.grad afresh on
+ * every step, triton_adam.py:137-153).  Every address must be 16-byte aligned
+ * (MAD_ERR_ALIGN otherwise: re-plan with mad_adamw_plan). */
+int mad_adamw_set_grads(void* dev_table, int64_t n_tiles, const void* const* grads, int32_t n_tensors, void* stream);
+
 /* One AdamW update of every planned tensor in one launch (replaces the
  * TritonAdamW.step per-tensor loop, triton_adam.py:132-153). */
 int mad_adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, float beta1, float beta2, float eps,
@@ -171,6 +179,11 @@ int mad_muon_plan_size(const mad_muon_matrix* mats, int32_t n_mats, mad_muon_pla
  * Synchronises `stream` once. */
 int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* dev_table, void* dev_work,
                   const mad_muon_plan_info* info, mad_muon_buffers* buffers, void* stream);
+
+/* mad_adamw_set_grads for a Muon plan: the gradient address of each planned
+ * matrix (grads[i] for matrix i), 16-byte aligned; no re-planning, no
+ * synchronisation (the reference reads p.grad afresh, triton_muon.py:414-448). */
+int mad_muon_set_grads(const mad_muon_plan_info* info, void* dev_table, const void* const* grads, void* stream);
 
 /* Momentum EMA, Nesterov, bf16 cast, transpose-to-wide and the Frobenius
  * norm of every planned matrix, in one launch. */

@@ -158,24 +158,41 @@ def frobenius_normalize(x: torch.Tensor, eps: float) -> tuple[torch.Tensor, floa
     return bf16_round(x / torch.tensor(norm, dtype=torch.float32)), norm
 
 
-def ns_iteration(x: torch.Tensor, a: float, b: float, c: float) -> torch.Tensor:
+def ns_iteration(x: torch.Tensor, a: float, b: float, c: float, triton_scalars: bool = False) -> torch.Tensor:
     """One Newton-Schulz iteration (triton_muon.py:313-325).
 
-    Each product is bf16 x bf16 accumulated wide and rounded once to bf16, the
-    way the three reference kernels do it:
+    Each product is bf16 x bf16 accumulated wide and rounded once to bf16, as
+    ``torch.optim.Muon`` (the wrapper's path) does it:
 
     * ``A  = bf16(X Xᵀ)``                 -- ns_kernel_1, triton_muon.py:35-93
     * ``B  = bf16(b A + c (A Aᵀ))``       -- ns_kernel_2, triton_muon.py:119-188
     * ``X' = bf16(a X + B X)``            -- ns_kernel_3, triton_muon.py:215-278
+
+    ``triton_scalars=True`` models the reference's Triton kernels exactly:
+    there ``b_coeff * A`` (:182) and ``a_coeff * X`` (:275) multiply a float
+    ``tl.constexpr`` by a bf16 block, and Triton's scalar promotion keeps such
+    a product in the tensor's type -- the coefficient is rounded to bf16
+    (a = 3.4445 -> 3.4375, b = -4.775 -> -4.78125) and the product is rounded
+    to bf16 before the float32 accumulator is added.  ``c_coeff * acc`` meets a
+    float32 block and stays float32.  (Pinned against the reference kernels on
+    the GPU by tests/test_gpu_reference.py.)
     """
     xd = x.double()
     A = bf16_round((xd @ xd.t()).float())
     Ad = A.double()
+    if triton_scalars:
+        ah, bh = float(bf16_round(torch.tensor(a))), float(bf16_round(torch.tensor(b)))
+        c32 = float(torch.tensor(c, dtype=torch.float32))
+        bA = bf16_round((bh * Ad).float()).double()
+        B = bf16_round((bA + c32 * (Ad @ Ad.t())).float())
+        aX = bf16_round((ah * xd).float()).double()
+        return bf16_round((aX + B.double() @ xd).float())
     B = bf16_round((b * Ad + c * (Ad @ Ad.t())).float())
     return bf16_round((a * xd + B.double() @ xd).float())
 
 
-def orthogonalize(u: torch.Tensor, coeffs, ns_steps: int, eps: float, normalize: str = "reference") -> torch.Tensor:
+def orthogonalize(u: torch.Tensor, coeffs, ns_steps: int, eps: float, normalize: str = "reference",
+                  triton_scalars: bool = False) -> torch.Tensor:
     """bf16 orthogonalised update in the parameter's orientation (triton_muon.py:351-366).
 
     ``normalize="reference"`` rounds ``X/||X||`` to bf16 before the first
@@ -185,15 +202,19 @@ def orthogonalize(u: torch.Tensor, coeffs, ns_steps: int, eps: float, normalize:
     (by s) before their bf16 roundings.  The two orderings differ only by bf16
     rounding placement (about 1-2% relative on small matrices, more on tiny
     ones), which is why tests hold the CUDA path tightly to "fold" and to the
-    reference tolerance against "reference".
+    reference tolerance against "reference".  ``triton_scalars`` (with
+    ``normalize="reference"``) applies the reference Triton kernels' bf16
+    rounding of ``a``, ``b`` and of their products (see ``ns_iteration``).
     """
     a, b, c = coeffs
     x, transposed = to_wide_bf16(u)
     if normalize == "reference":
         x, _ = frobenius_normalize(x, eps)
         for _ in range(ns_steps):
-            x = ns_iteration(x, a, b, c)
+            x = ns_iteration(x, a, b, c, triton_scalars)
     elif normalize == "fold":
+        if triton_scalars:
+            raise ValueError("triton_scalars models the reference Triton path, which normalises first")
         sumsq = float((x.double() * x.double()).sum())
         norm = float(bf16_round(torch.tensor(math.sqrt(sumsq), dtype=torch.float32)))
         norm = max(norm, float(bf16_round(torch.tensor(eps, dtype=torch.float32))))

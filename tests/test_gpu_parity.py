@@ -323,3 +323,41 @@ def test_step_from_host_matches_step(cuda_device):
         for p, q in zip(a, b):
             assert torch.equal(p.detach(), q.detach())
     assert oa.device_status() == 0 and ob.device_status() == 0
+
+
+def test_fresh_gradient_tensors_every_step_patch_the_plan_without_replanning(cuda_device):
+    """New ``.grad`` tensors every step (``zero_grad(set_to_none=True)`` + backward) give the results of
+    reused ones, with the gradient addresses patched in place: one plan per branch, built once."""
+    from triton_muon_adamw import AdamConfig, MuonAdamW, MuonConfig
+    gen = torch.Generator().manual_seed(41)
+    adam_shapes, muon_shapes = [(300, 64), (64,), (7,)], [(256, 64), (64, 256), (512, 512), (96, 200)]
+    init = [torch.randn(s, generator=gen) * 0.02 for s in adam_shapes + muon_shapes]
+    mc, ac = MuonConfig(coeffs=COEFFS), AdamConfig(lr=3e-4)
+    na = len(adam_shapes)
+    a = [torch.nn.Parameter(t.clone().to(cuda_device)) for t in init]
+    b = [torch.nn.Parameter(t.clone().to(cuda_device)) for t in init]
+    oa = MuonAdamW({"adam": a[:na], "muon": a[na:]}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+    ob = MuonAdamW({"adam": b[:na], "muon": b[na:]}, muon_config=mc, adam_config=ac, parameter_split="explicit")
+    for p in b:
+        p.grad = torch.zeros_like(p)
+    keep = []
+    for step in range(4):
+        grads = [(torch.randn(t.shape, generator=gen) * 1e-3).to(cuda_device) for t in init]
+        keep.append([torch.empty_like(g) for g in grads])      # keeps the allocator from handing back old blocks
+        for p, g in zip(a, grads):
+            p.grad = g.clone()                                  # a fresh tensor at a new address
+        for p, g in zip(b, grads):
+            p.grad.copy_(g)                                     # same tensors as last step
+        if step == 3:
+            # an unaligned gradient (a view one element into a buffer): refused by the patch, re-planned
+            buf = torch.empty(a[na].numel() + 1, device=cuda_device)
+            buf[1:].copy_(grads[na].reshape(-1))
+            a[na].grad = buf[1:].view_as(a[na])
+        oa.step()
+        ob.step()
+        torch.cuda.synchronize()
+        for p, q in zip(a, b):
+            assert torch.equal(p.detach(), q.detach()), f"step {step}: {tuple(p.shape)}"
+    assert oa.adamw._table.replans == 1, "AdamW table re-planned although only gradient addresses changed"
+    assert oa.muon._plan.replans == 2, "Muon plan: one plan, then one re-plan for the unaligned gradient only"
+    assert oa.device_status() == 0

@@ -104,7 +104,10 @@ def test_c1_gpt_many_steps_vs_reference_wrapper_and_reference_triton(cuda_device
             torch.testing.assert_close(p.detach(), q.detach(), atol=1e-2, rtol=1e-2)
             torch.testing.assert_close(p.detach(), r.detach(), atol=1e-2, rtol=1e-2)
         assert rec["muon_disp_rel_vs_wrapper"] < 3e-2, rec
-        assert rec["muon_disp_rel_vs_ref_triton"] < 3e-2, rec
+        # The reference's Triton kernels round a, b and their products to bf16 (see the NS tests
+        # below), which moves them further from torch.optim.Muon than ours: ours must stay at least
+        # as close to the wrapper as the reference's own Triton path is.
+        assert rec["muon_disp_rel_vs_wrapper"] <= rec["ref_triton_disp_rel_vs_wrapper"], rec
     if os.environ.get("MAD_PARITY_LOG"):
         with open(os.environ["MAD_PARITY_LOG"], "w") as f:
             json.dump({"config": "C1 17M GPT, fixed gradients", "drift": drift}, f, indent=1)
@@ -112,9 +115,116 @@ def test_c1_gpt_many_steps_vs_reference_wrapper_and_reference_triton(cuda_device
     assert o.device_status() == 0
 
 
+def _orthogonalize_gpu(u, coeffs, ns_steps, eps, normalize="fold", triton_scalars=False):
+    """``oracle.muon_adamw_oracle.orthogonalize`` restated on the GPU in float64.
+
+    Same rounding points: bf16 cast and transpose-to-wide, the bf16 norm of X
+    clamped at bf16(eps), every product accumulated in float64 and rounded to
+    bf16 once.  ``normalize="fold"``: s = float32(1/norm) folded into the first
+    Gram (s²) and the first update (s) -- the CUDA path's ordering.
+    ``"reference"``: X/norm rounded to bf16 first.  ``triton_scalars``: the
+    reference Triton kernels' bf16 rounding of a, b and of a·X, b·A
+    (``oracle.muon_adamw_oracle.ns_iteration``).
+    """
+    a, b, c = coeffs
+    x = u.to(torch.bfloat16).float()
+    tall = x.shape[0] > x.shape[1]
+    if tall:
+        x = x.t().contiguous()
+    xd = x.double()
+    norm = float(torch.tensor(math.sqrt(float((xd * xd).sum()))).to(torch.bfloat16).float())
+    norm = max(norm, float(torch.tensor(eps).to(torch.bfloat16).float()))
+
+    def r(t):
+        return t.float().to(torch.bfloat16).double()
+
+    if normalize == "fold":
+        s = float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(norm, dtype=torch.float32))
+    else:
+        xd = r(xd.float() / torch.tensor(norm, dtype=torch.float32))
+        s = 1.0
+    if triton_scalars:
+        a_h, b_h = float(bf16_round(torch.tensor(a))), float(bf16_round(torch.tensor(b)))
+        c_32 = float(torch.tensor(c, dtype=torch.float32))
+    for it in range(ns_steps):
+        s1 = s if it == 0 else 1.0
+        A = r((s1 * s1) * (xd @ xd.t()))
+        if triton_scalars:
+            B = r(r(b_h * A) + c_32 * (A @ A))
+            xd = r(r(a_h * xd) + B @ xd)
+        else:
+            B = r(b * A + c * (A @ A))
+            xd = r(s1 * (a * xd + B @ xd))
+    out = xd.float()
+    return out.t() if tall else out
+
+
+def _fold_orthogonalize_gpu(u, coeffs, ns_steps, eps):
+    return _orthogonalize_gpu(u, coeffs, ns_steps, eps, normalize="fold")
+
+
+def _frac_equal(model, got):
+    """Fraction of elements where the float64 model, rounded to bf16, equals the kernel's bf16 output."""
+    return float((model.float().to(torch.bfloat16) == got).float().mean())
+
+
+def test_reference_triton_kernels_round_their_scalar_coefficients_to_bf16(cuda_device):
+    """The reference's three NS kernels (triton_muon.py:35-310), run on the GPU, against float64 models.
+
+    ``ns_kernel_2`` forms ``b_coeff * A`` and ``ns_kernel_3`` ``a_coeff * X``
+    from a float ``tl.constexpr`` and a bf16 block: Triton keeps such products
+    in bf16, so the coefficient and the product are rounded to bf16 before the
+    float32 accumulator is added.  The model with that rounding
+    (``oracle.ns_iteration(triton_scalars=True)``) reproduces the kernels'
+    outputs bit for bit on nearly every element; the exact-coefficient model
+    does not.  This pins the oracle to the reference's Triton kernels directly.
+    """
+    R = load_reference()
+    T = R.muon.triton_muon
+    a, b, c = COEFFS
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+    m, n = 320, 704
+    x = (torch.randn(m, n, device=cuda_device, generator=gen) / math.sqrt(m * n) * 1.3).to(torch.bfloat16)
+    A = torch.empty(m, m, device=cuda_device, dtype=torch.bfloat16)
+    B = torch.empty_like(A)
+    X2 = torch.empty_like(x)
+    T.solve_ns_kernel_1(x, A)
+    T.solve_ns_kernel_2(A, b, c, B)
+    T.solve_ns_kernel_3(x, B, a, X2)
+    torch.cuda.synchronize()
+    xd, Ad, Bd = x.double(), A.double(), B.double()
+    a_h, b_h = float(bf16_round(torch.tensor(a))), float(bf16_round(torch.tensor(b)))
+    c_32 = float(torch.tensor(c, dtype=torch.float32))
+
+    def r(t):
+        return t.float().to(torch.bfloat16).double()
+
+    fr = {"gram": _frac_equal(xd @ xd.t(), A),
+          "poly_triton_scalars": _frac_equal(r(b_h * Ad) + c_32 * (Ad @ Ad), B),
+          "poly_exact": _frac_equal(b * Ad + c * (Ad @ Ad), B),
+          "update_triton_scalars": _frac_equal(r(a_h * xd) + Bd @ xd, X2),
+          "update_exact": _frac_equal(a * xd + Bd @ xd, X2)}
+    print(json.dumps({"bit_equal_fraction": fr}))
+    assert fr["gram"] > 0.99, fr
+    assert fr["poly_triton_scalars"] > 0.99 and fr["update_triton_scalars"] > 0.99, fr
+    assert fr["poly_exact"] < fr["poly_triton_scalars"] - 0.05, fr
+    assert fr["update_exact"] < fr["update_triton_scalars"] - 0.05, fr
+
+
 @pytest.mark.parametrize("shape", [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)])
 def test_reference_triton_newton_schulz_on_8b_shapes(cuda_device, shape):
-    """One TritonMuon.step of the reference's Triton kernels against one of ours, identical inputs."""
+    """One TritonMuon.step of the reference's Triton kernels against one of ours, identical inputs.
+
+    * the reference's update vs the oracle's model of its Triton path
+      (reference normalisation order, bf16-rounded scalars): < 1.2e-2 -- the
+      oracle is pinned to the reference kernels at full 8B size;
+    * ours vs the oracle with the stated coefficients (folded normalisation):
+      < 1.2e-2;
+    * a realistic step (lr 1e-3, wd 0.1, seeded parameter): ours equals the
+      reference's within its Muon tolerance, atol/rtol 1e-2 (README.md:52).
+    The remaining ours-vs-reference difference on the bare update is the
+    reference's bf16 coefficient rounding; it is recorded, not bounded.
+    """
     from triton_muon_adamw.muon import TritonMuon
     R = load_reference()
     RefMuon = R.muon.triton_muon.TritonMuon
@@ -133,40 +243,22 @@ def test_reference_triton_newton_schulz_on_8b_shapes(cuda_device, shape):
         cls([pr], lr=1e-3, weight_decay=0.1, coeffs=COEFFS, nesterov=True, ns_steps=5).step()
         results[name] = (-pz.detach() / scaled_lr(1.0, shape, "original"), pr.detach())
     (o_ours, p_ours), (o_ref, p_ref) = results["ours"], results["ref"]
-    err = float((o_ours - o_ref).norm() / o_ref.norm())
-    assert err < 2e-2, f"{shape}: orthogonalised update vs reference Triton, rel Frobenius {err:.3e}"
+    # First step from zero momentum: mom = 0.05 g; Nesterov u = g + 0.95 (mom - g), float32 as both compute it.
+    mom = g * torch.tensor(1.0 - 0.95, dtype=torch.float32).item()
+    u = g + (mom - g) * 0.95
+    m_tri = _orthogonalize_gpu(u, COEFFS, 5, 1e-7, normalize="reference", triton_scalars=True)
+    m_fold = _orthogonalize_gpu(u, COEFFS, 5, 1e-7, normalize="fold")
+
+    def rel(x, y):
+        return float((x - y).norm() / y.norm())
+
+    rec = {"shape": list(shape), "ref_triton_vs_oracle_triton_model": rel(o_ref, m_tri),
+           "ours_vs_oracle_fold": rel(o_ours, m_fold), "ours_vs_ref_triton": rel(o_ours, o_ref),
+           "oracle_fold_vs_oracle_triton_model": rel(m_fold, m_tri)}
+    print(json.dumps(rec))
+    assert rec["ref_triton_vs_oracle_triton_model"] < 1.2e-2, rec
+    assert rec["ours_vs_oracle_fold"] < 1.2e-2, rec
     torch.testing.assert_close(p_ours, p_ref, atol=1e-2, rtol=1e-2)
-    print(json.dumps({"shape": list(shape), "update_rel_frobenius_vs_ref_triton": err}))
-
-
-def _fold_orthogonalize_gpu(u, coeffs, ns_steps, eps):
-    """``oracle.muon_adamw_oracle.orthogonalize(normalize="fold")`` restated on the GPU in float64.
-
-    Same rounding points: bf16 cast and transpose-to-wide, the bf16 norm of X
-    clamped at bf16(eps), s = float32(1/norm) folded into the first Gram (s²)
-    and the first update (s), every product accumulated in float64 and
-    rounded to bf16 once.
-    """
-    a, b, c = coeffs
-    x = u.to(torch.bfloat16).float()
-    tall = x.shape[0] > x.shape[1]
-    if tall:
-        x = x.t().contiguous()
-    xd = x.double()
-    norm = float(torch.tensor(math.sqrt(float((xd * xd).sum()))).to(torch.bfloat16).float())
-    norm = max(norm, float(torch.tensor(eps).to(torch.bfloat16).float()))
-    s = float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(norm, dtype=torch.float32))
-
-    def r(t):
-        return t.float().to(torch.bfloat16).double()
-
-    for it in range(ns_steps):
-        s1 = s if it == 0 else 1.0
-        A = r((s1 * s1) * (xd @ xd.t()))
-        B = r(b * A + c * (A @ A))
-        xd = r(s1 * (a * xd + B @ xd))
-    out = xd.float()
-    return out.t() if tall else out
 
 
 def test_gpu_fold_restatement_matches_the_cpu_oracle(cuda_device):

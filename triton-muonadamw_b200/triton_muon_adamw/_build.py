@@ -18,7 +18,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE.parent / "csrc"
 INCLUDE = HERE.parent.parent / "include"
 OUT = HERE / "libmuonadamw_b200.so"
-SOURCES = ["capi.cu", "adamw.cu", "muon_prep.cu", "ns_gemm.cu", "muon_plan.cu", "muon_noalloc.cu", "p2p.cu"]
+SOURCES = ["capi.cu", "adamw.cu", "muon_prep.cu", "ns_gemm.cu", "muon_plan.cu", "muon_noalloc.cu", "p2p.cu", "patch.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

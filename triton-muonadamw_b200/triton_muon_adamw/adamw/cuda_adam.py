@@ -64,16 +64,36 @@ class AdamWTable:
 
     def __init__(self):
         self.key = None
+        self.grads = None
         self.table = None
         self.n_tiles = 0
         self.numel = 0
+        self.replans = 0
 
     def ensure(self, quads, device) -> None:
+        """Plan (or keep) the table for these tensors.
+
+        The key leaves the gradient addresses out: when only they changed (new
+        ``.grad`` tensors after ``zero_grad(set_to_none=True)``), they are
+        rewritten in place on the stream (``mad_adamw_set_grads``) instead of
+        re-planning, as long as the old and the new addresses are all 16-byte
+        aligned (the planned vector width stays legal and optimal).
+        """
         quads = [tuple(q) + (None,) * (5 - len(q)) for q in quads]
-        key = tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), p.dtype,
+        key = tuple((p.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), p.dtype, g.dtype,
                      sh.data_ptr() if sh is not None else 0) for p, g, m, v, sh in quads)
+        grads = tuple(q[1].data_ptr() for q in quads)
         if key == self.key:
-            return
+            if grads != self.grads:
+                if all(a % 16 == 0 for a in grads) and all(a % 16 == 0 for a in self.grads):
+                    lib = _lib.load()
+                    arr = (ctypes.c_void_p * max(1, len(grads)))(*grads)
+                    _lib.check(lib.mad_adamw_set_grads(self.table.data_ptr(), self.n_tiles, arr, len(grads),
+                                                       _lib.stream_handle()), "mad_adamw_set_grads")
+                    self.grads = grads
+                    return
+            else:
+                return
         lib = _lib.load()
         arr = (_lib.AdamWTensor * max(1, len(quads)))()
         for i, (p, g, m, v, sh) in enumerate(quads):
@@ -89,6 +109,8 @@ class AdamWTable:
         self.n_tiles = n_tiles.value
         self.numel = sum(q[0].numel() for q in quads)
         self.key = key
+        self.grads = grads
+        self.replans += 1
 
     def launch(self, *, lr, beta1, beta2, eps, weight_decay, bias1, bias2, reduce=None) -> None:
         """One launch over the table; ``reduce`` (a ``GradReduce``) sums each gradient over ranks."""

@@ -53,6 +53,8 @@ class MuonPlan:
 
     def __init__(self):
         self.key = None
+        self.grads = None
+        self.replans = 0
         self.info = _lib.MuonPlanInfo()
         self.table = None
         self.work = None
@@ -61,11 +63,27 @@ class MuonPlan:
         self.shapes = []
 
     def ensure(self, triples, adjust_lr_fn, device) -> None:
+        """Plan (or keep) the plan for these matrices.
+
+        Gradient addresses are not part of the key: when only they changed,
+        ``mad_muon_set_grads`` rewrites them in place on the stream (old and
+        new addresses all 16-byte aligned) -- no tensor-map encodes, no upload,
+        no synchronisation.
+        """
         triples = [tuple(t) + (None,) * (4 - len(t)) for t in triples]
-        key = (adjust_lr_fn,) + tuple((p.data_ptr(), g.data_ptr(), m.data_ptr(), tuple(p.shape), p.dtype,
+        key = (adjust_lr_fn,) + tuple((p.data_ptr(), m.data_ptr(), tuple(p.shape), p.dtype, g.dtype,
                                        sh.data_ptr() if sh is not None else 0) for p, g, m, sh in triples)
+        grads = tuple(t[1].data_ptr() for t in triples)
         if key == self.key:
-            return
+            if grads == self.grads:
+                return
+            if all(a % 16 == 0 for a in grads) and all(a % 16 == 0 for a in self.grads):
+                lib = _lib.load()
+                arr = (ctypes.c_void_p * max(1, len(grads)))(*grads)
+                _lib.check(lib.mad_muon_set_grads(ctypes.byref(self.info), self.table.data_ptr(), arr,
+                                                  _lib.stream_handle()), "mad_muon_set_grads")
+                self.grads = grads
+                return
         lib = _lib.load()
         n = len(triples)
         arr = (_lib.MuonMatrix * max(1, n))()
@@ -89,6 +107,8 @@ class MuonPlan:
         self.n_mats = n
         self.shapes = [tuple(t[0].shape) for t in triples]
         self.key = key
+        self.grads = grads
+        self.replans += 1
 
     def read_status(self, clear=True) -> int:
         st = ctypes.c_uint32(0)
