@@ -196,6 +196,12 @@ def ns_flops_sym(shape):
     return {"gram": float(m) * m * n, "poly": float(m) ** 3, "update": 2.0 * m * m * n}
 
 
+# Launches of each NS phase per step: ns_steps of Gram and polynomial, ns_steps - 1 plain updates
+# and one last update (which writes the parameters).
+def ns_phase_launches(phase, ns_steps):
+    return {"gram": ns_steps, "poly": ns_steps, "update": ns_steps - 1, "update_last": 1}[phase]
+
+
 # ----------------------------------------------------------------- CPU baseline
 def cpu_sample(cfg_key, adam_cfg, ns_steps):
     """Time the reference's CPU path on one matrix per distinct Muon shape + an AdamW chunk; extrapolate."""
@@ -240,7 +246,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="8b", choices=sorted(CONFIGS) + list(SWEEPS),
+                    help="8b (default: the Llama-3-8B-shaped step), 1b3, prof (small ncu case), or the "
+                         "isolated sweeps adamw_sweep (C2) and ns_isolated (C3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -257,6 +265,10 @@ def main():
     ap.add_argument("--no-verify", action="store_true",
                     help="at N>1, skip the post-timing check of every replica against a single-GPU recomputation")
     args = ap.parse_args()
+    if args.config in SWEEPS:
+        if int(os.environ.get("RANK", "0")) == 0:
+            SWEEPS[args.config](args)
+        return
     cfg = CONFIGS[args.config]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -351,12 +363,12 @@ def main():
 
     # Work accounting (this rank's share), per step.
     owned = owned_shapes(opt)
-    flops = {"gram": 0.0, "poly": 0.0, "update": 0.0}
+    flops = {"gram": 0.0, "poly": 0.0, "update": 0.0, "update_last": 0.0}
     elems_muon = 0
     for s in owned:
         f = ns_flops_sym(s)
         for k in flops:
-            flops[k] += f[k] * args.ns_steps
+            flops[k] += f["update" if k == "update_last" else k] * ns_phase_launches(k, args.ns_steps)
         elems_muon += math.prod(s)
     adam_elems = adam_elems_local(opt)
     hbm, tf_burst, tf_sus, peak_src = measured_peaks()
@@ -366,7 +378,7 @@ def main():
         d = per.get(label, [])
         return (sum(d) / timing_steps, len(d) / timing_steps) if d else (0.0, 0.0)
 
-    for k in ("gram", "poly", "update"):
+    for k in ("gram", "poly", "update", "update_last"):
         ms_k, n_k = phase(k)
         if n_k:
             tfl = flops[k] / (ms_k * 1e-3) / 1e12
@@ -381,9 +393,9 @@ def main():
     ms_p, n_p = phase("prep")
     if n_p:
         gbs = 14.0 * elems_muon / (ms_p * 1e-3) / 1e9
-        kernels["muon_prep"] = {"launches_per_step": n_p, "ms_per_step": round(ms_p, 3), "gbs": round(gbs, 1),
+        kernels["muon_prep"] = {"launches_per_step": 2 * n_p, "includes": "muon_norm_kernel", "ms_per_step": round(ms_p, 3), "gbs": round(gbs, 1),
                                 "frac": round(gbs / hbm, 3), "bytes_per_elem": 14}
-    ns_ms = sum(phase(k)[0] for k in ("gram", "poly", "update"))
+    ns_ms = sum(phase(k)[0] for k in ("gram", "poly", "update", "update_last"))
     ns_total = sum(flops.values())
     upd = kernels.get("ns_gemm_update", {})
     traffic, traffic_how = ncu_traffic("ns_gemm_update", args.config)
@@ -393,7 +405,9 @@ def main():
                 "traffic": traffic, "traffic_source": traffic_how, "ns_all_tflops": round(ns_total / (ns_ms * 1e-3) / 1e12, 1) if ns_ms else None,
                 "ns_all_frac_sustained": round(ns_total / (ns_ms * 1e-3) / 1e12 / tf_sus, 3) if ns_ms else None,
                 "ns_ms_per_step": round(ns_ms, 3), "ns_flops_per_step": ns_total}
-    launches_per_step = sum(len(v) for v in per.values()) / timing_steps
+    # Kernel launches per timed phase: the prep phase is the prep kernel plus the per-matrix norm kernel.
+    kernels_per_phase = {"prep": 2}
+    launches_per_step = sum(len(v) * kernels_per_phase.get(k, 1) for k, v in per.items()) / timing_steps
 
     # At N>1: one more (untimed) step, checked -- replicas bit-identical on every rank, and rank 0
     # recomputes matrices and AdamW tensors owned by other ranks with the single-GPU optimizer.
@@ -591,7 +605,7 @@ def run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier):
     opt.close()
     return {"fused_step_ms": round(fused, 3), "nccl_allreduce_ms": round(allreduce, 3),
             "gradient_bytes_per_rank": int(arena.numel()), "reduce_kernels": peer,
-            "gemm_ms_per_step": round(sum(phases.get(k, 0.0) for k in ("gram", "poly", "update")), 3),
+            "gemm_ms_per_step": round(sum(phases.get(k, 0.0) for k in ("gram", "poly", "update", "update_last")), 3),
             "what": "step with per-rank gradients summed inside the AdamW/Muon-prep kernels (peer loads over "
                     "NVLink) vs the NCCL all-reduce (AVG) of the same gradient bytes that a step on reduced "
                     "gradients needs first; compare fused_step_ms with nccl_allreduce_ms + value"}
@@ -816,6 +830,150 @@ def run_reference_triton_arm(args, cfg, world, local_rank):
                        "source": "reference package, unmodified, from baseline/_ref"},
             "clocks": clock_info}
     print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- isolated sweeps (C2, C3)
+def _event_ms(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def run_adamw_sweep(args):
+    """C2: the AdamW branch alone on flat float32 tensors of 1M, 16M, 64M and 256M elements and on 10,000
+    ragged tensors of 1..65536 elements (seeded; ~3.3e8 elements), moments from 5 warm-up steps.
+
+    Per case: our one-launch multi-tensor step (``TritonAdamW``), the reference's own ``TritonAdamW`` (one
+    Triton launch per tensor, from baseline/_ref) and ``torch.optim.AdamW(fused=True)``, all on this GPU
+    with CUDA events; GB/s = 28 B/element / time, against the measured HBM copy bandwidth.  Inputs of the
+    large cases exceed L2; the 1M case fits in L2 (reported as is)."""
+    import importlib.util  # noqa: PLC0415
+    from triton_muon_adamw.adamw import TritonAdamW  # noqa: PLC0415
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, _, _, peak_src = measured_peaks()
+    ref_mod = None
+    init = ROOT / "baseline" / "_ref" / "triton_muon_adamw" / "__init__.py"
+    if init.exists():
+        spec = importlib.util.spec_from_file_location("ref_triton_muon_adamw", init,
+                                                      submodule_search_locations=[str(init.parent)])
+        ref_mod = importlib.util.module_from_spec(spec)
+        sys.modules["ref_triton_muon_adamw"] = ref_mod
+        spec.loader.exec_module(ref_mod)
+    hp = dict(lr=3e-4, betas=(0.9, 0.999), weight_decay=0.01, eps=1e-8)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    cases = [("1M", [1 << 20]), ("16M", [1 << 24]), ("64M", [1 << 26]), ("256M", [1 << 28])]
+    rg = torch.Generator().manual_seed(7)
+    cases.append(("ragged_10k", torch.randint(1, 65537, (10000,), generator=rg).tolist()))
+    out = []
+    for name, sizes in cases:
+        numel = sum(sizes)
+        row = {"case": name, "tensors": len(sizes), "elements": numel, "bytes_per_step": 28 * numel}
+        impls = [("ours", lambda ps: TritonAdamW(ps, **hp))]
+        if ref_mod is not None:
+            impls.append(("reference_triton", lambda ps: ref_mod.adamw.triton_adam.TritonAdamW(ps, **hp)))
+        impls.append(("torch_fused", lambda ps: torch.optim.AdamW(ps, fused=True, **hp)))
+        for impl, make in impls:
+            # The reference launches grid (rows, cdiv(cols, 512)) per tensor (triton_adam.py:92-94), and a 1-D
+            # tensor is one row: beyond 65535 * 512 elements grid.y exceeds the CUDA limit and the launch fails.
+            # It runs those cases on the same elements viewed as rows of 4096 (the update is elementwise).
+            as_rows = impl == "reference_triton" and max(sizes) > 65535 * 512
+            if as_rows:
+                row["reference_triton_layout"] = "rows of 4096 (a flat tensor this long exceeds its grid limit)"
+            params = [nn.Parameter(torch.empty((n // 4096, 4096) if as_rows and n % 4096 == 0 else (n,), device=dev)
+                                   .normal_(0, 0.02, generator=gen)) for n in sizes]
+            for q in params:
+                q.grad = torch.empty_like(q).normal_(0, 1e-2, generator=gen)
+            opt = make(params)
+            for _ in range(5):                       # moments from 5 warm-up steps
+                opt.step()
+            ms = _event_ms(opt.step, max(3, args.steps), 2)
+            gbs = 28.0 * numel / (ms * 1e-3) / 1e9
+            row[impl] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
+            del opt, params
+            torch.cuda.empty_cache()
+        if "reference_triton" in row:
+            row["speedup_vs_reference_triton"] = round(row["reference_triton"]["ms"] / row["ours"]["ms"], 2)
+        row["speedup_vs_torch_fused"] = round(row["torch_fused"]["ms"] / row["ours"]["ms"], 2)
+        out.append(row)
+        print(json.dumps(row), file=sys.stderr, flush=True)
+    big = next(r for r in out if r["case"] == "256M")
+    print(json.dumps({"metric": "AdamW HBM GB/s (C2 sweep; value: 256M-element case)", "value": big["ours"]["gbs"],
+                      "unit": "GB/s", "higher_is_better": True, "n_gpus": 1, "steps": max(3, args.steps),
+                      "dtype": "fp32", "data": "synthetic (seeded; params N(0,0.02), grads N(0,1e-2))",
+                      "peak": hbm, "peak_kind": f"{peak_src} HBM copy", "config": {"workload": "C2 AdamW sweep"},
+                      "cases": out}), flush=True)
+
+
+def run_ns_sweep(args):
+    """C3: Newton-Schulz in isolation -- bf16-valued N(0,1) matrices of 1024x1024, 4096x4096, 4096x14336 and
+    14336x4096 (tall: transposed), batches of 1, 8 and 32 in one plan, ns_steps 5 and 6.
+
+    One ``TritonMuon`` step per timed iteration (beta=0, no Nesterov: X is the gradient itself), its
+    launches timed with CUDA events on the launching stream; TFLOP/s over the Gram, polynomial and update
+    GEMMs = (3m^2n + m^3 per iteration, triangles counted once) / their time, against the measured
+    sustained bf16 peak; the dense-equivalent 4m^2n + 2m^3 rate is reported beside it."""
+    from triton_muon_adamw.muon import TritonMuon  # noqa: PLC0415
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _, tf_burst, tf_sus, peak_src = measured_peaks()
+    gen = torch.Generator(device=dev).manual_seed(0)
+    out = []
+    for shape in [(1024, 1024), (4096, 4096), (4096, 14336), (14336, 4096)]:
+        for batch in (1, 8, 32):
+            for ns in (5, 6):
+                params = []
+                for _ in range(batch):
+                    q = nn.Parameter(torch.zeros(shape, device=dev))
+                    q.grad = torch.empty(shape, device=dev).normal_(0, 1, generator=gen).bfloat16().float()
+                    params.append(q)
+                opt = TritonMuon(params, lr=1e-3, weight_decay=0.0, coeffs=COEFFS, nesterov=False, beta=0.0,
+                                 ns_steps=ns, eps=1e-7)
+                for _ in range(2):
+                    opt.step()
+                timer = PhaseTimer()
+                opt._timer = timer
+                steps = max(2, min(args.steps, 5))
+                torch.cuda.synchronize()
+                for _ in range(steps):
+                    opt.step()
+                torch.cuda.synchronize()
+                opt._timer = None
+                per = timer.durations()
+                ns_ms = sum(sum(per.get(k, [])) for k in ("gram", "poly", "update", "update_last")) / steps
+                prep_ms = sum(per.get("prep", [])) / steps
+                m, n = min(shape), max(shape)
+                sym = batch * ns * (3.0 * m * m * n + float(m) ** 3)
+                dense = batch * ns * (4.0 * m * m * n + 2.0 * float(m) ** 3)
+                tf = sym / (ns_ms * 1e-3) / 1e12
+                row = {"shape": list(shape), "batch": batch, "ns_steps": ns, "ns_ms": round(ns_ms, 3),
+                       "prep_ms": round(prep_ms, 3), "tflops": round(tf, 1),
+                       "frac_sustained": round(tf / tf_sus, 3), "frac_burst": round(tf / tf_burst, 3),
+                       "dense_equiv_tflops": round(dense / (ns_ms * 1e-3) / 1e12, 1)}
+                st = opt.device_status()
+                if st:
+                    row["device_status"] = st
+                out.append(row)
+                print(json.dumps(row), file=sys.stderr, flush=True)
+                del opt, params
+                torch.cuda.empty_cache()
+    best = max(out, key=lambda r: r["tflops"])
+    head = next(r for r in out if r["shape"] == [4096, 14336] and r["batch"] == 32 and r["ns_steps"] == 5)
+    print(json.dumps({"metric": "Newton-Schulz TFLOP/s (C3; value: 32 x 4096x14336, ns 5)", "value": head["tflops"],
+                      "unit": "TFLOP/s", "higher_is_better": True, "n_gpus": 1, "dtype": "bf16 (fp32 accumulate)",
+                      "data": "synthetic (bf16-valued N(0,1) matrices, seeded)", "peak_sustained": tf_sus,
+                      "peak_burst": tf_burst, "peak_kind": f"{peak_src} bf16", "best_case": best,
+                      "config": {"workload": "C3 Newton-Schulz isolated"}, "cases": out}), flush=True)
+
+
+SWEEPS = {"adamw_sweep": run_adamw_sweep, "ns_isolated": run_ns_sweep}
 
 
 if __name__ == "__main__":

@@ -11,9 +11,12 @@
 //
 // Layout: a multi-tensor launch walks a table of tensors cut into 4096-element
 // tiles; a tile -> tensor index map (int32 per tile) sits in front of the
-// AdamEntry array, so each CTA finds its tensor with one load.  Each thread
-// moves 4 float4 of each of p, g, m, v per tile (16 B x 4 streams in flight),
-// which is what the HBM3e streaming roofline needs: 28 bytes per element.
+// AdamEntry array, so each CTA finds its tensor with one load (and loads the
+// next tile's entry while it works on the current one).  Each thread moves
+// ADAM_VECS float4 of each of p, g, m, v per tile; many small resident CTAs
+// (four per SM) keep the bytes in flight the HBM3e streaming roofline needs
+// -- 28 bytes per element -- and the warps to cover the division and
+// square-root chains at the power-capped SM clock.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -63,8 +66,8 @@ __device__ __forceinline__ void put1(TP* p, __nv_bfloat16* sh, int64_t i, float 
 }
 
 // The tile with the gradient summed over ranks.  Full tiles: each thread's
-// four vectors of every rank's copy, two ranks (8 vectors) in flight at a
-// time, then p, m, v; the remote reads cross NVLink, which bounds this path.
+// vectors of every rank's copy, two ranks' in flight at a time, then p, m, v;
+// the remote reads cross NVLink, which bounds this path.
 template <typename TP, typename TG, bool SHADOW>
 __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
   TP* __restrict__ p = static_cast<TP*>(e.p) + off;
@@ -74,13 +77,13 @@ __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off
   float* __restrict__ v = e.v + off;
   const int t = threadIdx.x;
   if (e.vec && len == ADAM_TILE) {
-    int64_t offs[4];
-    float4 gv[4];
+    int64_t offs[ADAM_VECS];
+    float4 gv[ADAM_VECS];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) offs[j] = 4 * static_cast<int64_t>(j * ADAM_THREADS + t);
-    ld4_ranks_rows<TG, 4>(g, offs, gv, s.red);
+    for (int j = 0; j < ADAM_VECS; ++j) offs[j] = 4 * static_cast<int64_t>(j * ADAM_THREADS + t);
+    ld4_ranks_rows<TG, ADAM_VECS>(g, offs, gv, s.red);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < ADAM_VECS; ++j) {
       const int idx = j * ADAM_THREADS + t;
       float4 a = ld4(p, idx);
       float4 c = __ldcs(reinterpret_cast<const float4*>(m) + idx);
@@ -113,7 +116,7 @@ __device__ __forceinline__ void adam_tile_reduce(const AdamEntry& e, int64_t off
 }
 
 // One tile [off, off+len) of one tensor: parameter type TP, gradient type TG,
-// float32 moments.  Full aligned tiles take the 16-loads-in-flight path;
+// float32 moments.  Full aligned tiles issue all their loads before any math;
 // ragged or misaligned pieces take a generic loop.
 template <typename TP, typename TG, bool SHADOW>
 __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int len, const AdamScalars& s) {
@@ -124,9 +127,9 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
   float* __restrict__ v = e.v + off;
   const int t = threadIdx.x;
   if (e.vec && len == ADAM_TILE) {
-    float4 rp[4], rg[4], rm[4], rv[4];
+    float4 rp[ADAM_VECS], rg[ADAM_VECS], rm[ADAM_VECS], rv[ADAM_VECS];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < ADAM_VECS; ++i) {
       const int idx = i * ADAM_THREADS + t;
       rp[i] = ld4(p, idx);
       rg[i] = ld4(g, idx);
@@ -134,7 +137,7 @@ __device__ __forceinline__ void adam_tile(const AdamEntry& e, int64_t off, int l
       rv[i] = __ldcs(reinterpret_cast<const float4*>(v) + idx);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < ADAM_VECS; ++i) {
       adam_vec(rp[i], rg[i], rm[i], rv[i], s);
       const int idx = i * ADAM_THREADS + t;
       put4<TP, SHADOW>(p, sh, idx, rp[i]);
@@ -183,19 +186,38 @@ __device__ __forceinline__ void adam_tile_any(const AdamEntry& e, int64_t off, i
 
 // REDUCE: the gradient summed over ranks (a separate instantiation, so the
 // local path keeps its register budget and occupancy).
+constexpr int ADAM_CTAS_PER_SM = 4;         // resident CTAs of the local-gradient kernel
+constexpr int ADAM_REDUCE_CTAS_PER_SM = 1;  // the rank-summing kernel's registers allow one
+
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)) : "memory");
+}
+
+// The next tile's table entry (two dependent loads: tile map, then entry) is
+// requested while the current tile is processed -- its index into a register,
+// its 64-byte entry into L1 -- so a CTA's data loads for a tile go out as soon
+// as it starts the tile.
 template <bool REDUCE>
-__global__ void __launch_bounds__(ADAM_THREADS) adamw_multi_kernel(
-    const AdamEntry* __restrict__ entries, const int32_t* __restrict__ tile_map, int64_t n_tiles, AdamScalars s) {
-  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-    const AdamEntry e = entries[tile_map[tile]];
+__global__ void __launch_bounds__(ADAM_THREADS, REDUCE ? ADAM_REDUCE_CTAS_PER_SM : ADAM_CTAS_PER_SM)
+    adamw_multi_kernel(const AdamEntry* __restrict__ entries, const int32_t* __restrict__ tile_map, int64_t n_tiles,
+                       AdamScalars s) {
+  int64_t tile = blockIdx.x;
+  if (tile >= n_tiles) return;
+  int32_t idx = tile_map[tile];
+  for (; tile < n_tiles; tile += gridDim.x) {
+    const AdamEntry e = entries[idx];
+    const int64_t next = tile + gridDim.x;
+    const int32_t next_idx = next < n_tiles ? __ldg(tile_map + next) : idx;
     const int64_t off = (tile - e.tile_begin) * ADAM_TILE;
     const int64_t rem = e.numel - off;
     const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
     adam_tile_any<REDUCE>(e, off, len, s);
+    if (threadIdx.x == 0) prefetch_l1(entries + next_idx);
+    idx = next_idx;
   }
 }
 
-__global__ void __launch_bounds__(ADAM_THREADS) adamw_single_kernel(AdamEntry e, int64_t n_tiles, AdamScalars s) {
+__global__ void __launch_bounds__(ADAM_THREADS, ADAM_CTAS_PER_SM) adamw_single_kernel(AdamEntry e, int64_t n_tiles, AdamScalars s) {
   for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
     const int64_t off = tile * ADAM_TILE;
     const int64_t rem = e.numel - off;
@@ -222,9 +244,9 @@ static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, f
   return s;
 }
 
-static int adam_grid(int64_t n_tiles) {
-  // 8 resident CTAs of 256 threads per SM; a grid-stride loop covers the rest.
-  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+static int adam_grid(int64_t n_tiles, int per_sm) {
+  // per_sm resident CTAs of 256 threads per SM, striding over the tiles.
+  const int64_t cap = static_cast<int64_t>(num_sms()) * per_sm;
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n_tiles, cap)));
 }
 
@@ -274,7 +296,7 @@ extern "C" int mad_adamw_step(float* param, const float* grad, float* exp_avg, f
   e.dtype = MAD_DTYPE_F32;
   e.vec = vec_ok(param, grad, exp_avg, exp_avg_sq, nullptr, MAD_DTYPE_F32);
   const int64_t n_tiles = (numel + ADAM_TILE - 1) / ADAM_TILE;
-  adamw_single_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+  adamw_single_kernel<<<adam_grid(n_tiles, ADAM_CTAS_PER_SM), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       e, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
   return check_launch("adamw_single_kernel");
 }
@@ -356,9 +378,11 @@ static int adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, fl
   const AdamEntry* entries = reinterpret_cast<const AdamEntry*>(base + entries_offset(n_tiles));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (sc.red.n > 0)
-    adamw_multi_kernel<true><<<adam_grid(n_tiles), ADAM_THREADS, 0, st>>>(entries, tile_map, n_tiles, sc);
+    adamw_multi_kernel<true><<<adam_grid(n_tiles, ADAM_REDUCE_CTAS_PER_SM), ADAM_THREADS, 0, st>>>(entries, tile_map,
+                                                                                                 n_tiles, sc);
   else
-    adamw_multi_kernel<false><<<adam_grid(n_tiles), ADAM_THREADS, 0, st>>>(entries, tile_map, n_tiles, sc);
+    adamw_multi_kernel<false><<<adam_grid(n_tiles, ADAM_CTAS_PER_SM), ADAM_THREADS, 0, st>>>(entries, tile_map,
+                                                                                           n_tiles, sc);
   return check_launch("adamw_multi_kernel");
 }
 

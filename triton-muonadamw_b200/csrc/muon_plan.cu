@@ -21,8 +21,8 @@
 
 namespace mad {
 
-int launch_muon_prep(MatDesc* mats, const int32_t* prep_map, float* partials, int64_t n_tiles, double beta,
-                     int nesterov, float eps, const GradReduce& red, cudaStream_t stream);
+int launch_muon_prep(MatDesc* mats, int32_t n_mats, const int32_t* prep_map, float* partials, int64_t n_tiles,
+                     double beta, int nesterov, float eps, const GradReduce& red, cudaStream_t stream);
 int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, const TileRef* tiles, int64_t n_tiles,
                    int iter, int last, float a, float b, float c, double lr, float lr_wd, unsigned int* status,
                    cudaStream_t stream);
@@ -174,7 +174,7 @@ extern "C" int mad_muon_plan_size(const mad_muon_matrix* mats, int32_t n_mats, m
   pi.off_prep_map = off;
   off = round_up(off + pi.prep_tiles * 4, 256);
   pi.off_partials = off;
-  off = round_up(off + pi.prep_tiles * 4, 256);
+  off = round_up(off + pi.prep_tiles * 4 * PREP_PARTIALS_PER_TILE, 256);
   pi.table_bytes = off;
   pi.work_bytes = work;
   *info = pi;
@@ -345,7 +345,7 @@ static int muon_prep(const mad_muon_plan_info* info, void* dev_table, double bet
   if (int rc = grad_reduce_from(reduce, &red, who)) return rc;
   if (info->n_mats == 0) return MAD_OK;
   const Views v = views(info, dev_table);
-  return launch_muon_prep(v.mats, v.prep_map, v.partials, info->prep_tiles, beta, nesterov, eps, red,
+  return launch_muon_prep(v.mats, info->n_mats, v.prep_map, v.partials, info->prep_tiles, beta, nesterov, eps, red,
                           static_cast<cudaStream_t>(stream));
 }
 

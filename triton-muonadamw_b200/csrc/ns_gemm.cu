@@ -383,6 +383,37 @@ __device__ __forceinline__ void write_params(const MatDesc& md, const float (&v)
   }
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)) : "memory");
+}
+
+// UPDATE_LAST: pull the parameter block this warp will read and rewrite for a
+// tile -- X' rows grow0..grow0+31 x columns col0..col0+127 -- into L2 a tile
+// ahead, so the epilogue's parameter loads hit L2 instead of waiting on DRAM.
+// Only lines that hold parameter elements are touched.
+__device__ __forceinline__ void prefetch_param_block(const MatDesc& md, int grow0, int col0) {
+  const int lane = threadIdx.x & 31;
+  const int es = md.dtype == MAD_DTYPE_BF16 ? 2 : 4;
+  const char* base = static_cast<const char*>(md.p);
+  if (grow0 >= md.m || col0 >= md.n) return;
+  if (!md.transposed) {
+    // Parameter row grow0 + lane, columns col0 .. min(col0 + 128, n).
+    const int r = grow0 + lane;
+    if (r >= md.m) return;
+    const int cend = col0 + 128 < md.n ? col0 + 128 : md.n;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(base + (static_cast<int64_t>(r) * md.n + col0) * es);
+    const uintptr_t e = reinterpret_cast<uintptr_t>(base + (static_cast<int64_t>(r) * md.n + cend) * es);
+    for (uintptr_t l = a & ~static_cast<uintptr_t>(127); l < e; l += 128) prefetch_l2(reinterpret_cast<const void*>(l));
+  } else {
+    // Parameter rows col0 .. col0+127 (four per lane), columns grow0 .. grow0+31: one line each.
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int pr = col0 + 4 * lane + j;
+      if (pr < md.n) prefetch_l2(base + (static_cast<int64_t>(pr) * md.m + grow0) * es);
+    }
+  }
+}
+
 template <int MODE>
 __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc& md, int grow0, int grow, bool row_ok,
                                              int gcol0, bool mirror, uint32_t (&acc)[32], const ChunkIn& in,
@@ -439,6 +470,19 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   const int half = (warp - 2) >> 2;
   const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  // This warp's rows and columns of tile t: rows of its CTA's 128-row block, its quarter; its half of the columns.
+  auto warp_rows0 = [&](const TileRef& r) { return r.tm * PAIR_M + static_cast<int>(rank) * BM + quad * 32; };
+  auto warp_col0 = [&](const TileRef& r) { return r.tn * BN + half * 128; };
+  // UPDATE_LAST: this CTA's first two tiles now, then at the end of tile t the
+  // tile after next -- about a tile's mainloop of lead time.
+  auto prefetch_tile = [&](int tt) {
+    if (MODE == UPDATE_LAST && tt < args.n_tiles) {
+      const TileRef r = args.tiles[tt];
+      prefetch_param_block(args.mats[r.mat], warp_rows0(r), warp_col0(r));
+    }
+  };
+  prefetch_tile(cid);
+  prefetch_tile(cid + ncl);
   int lt = 0;
   for (int t = cid; t < args.n_tiles; t += ncl, ++lt) {
     const TileRef tr = args.tiles[t];
@@ -503,6 +547,7 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     __syncwarp();
     if (lane == 0) mbar_arrive_cluster(tempty_leader[acc_buf]);
     if (*abort_flag) break;
+    prefetch_tile(t + 2 * ncl);
   }
   if (lane == 0) bulk_wait_all();  // every output store has landed before the CTA retires
 }

@@ -30,7 +30,8 @@ struct AdamEntry {
 static_assert(sizeof(AdamEntry) == 64, "AdamEntry layout");
 
 constexpr int ADAM_THREADS = 256;
-constexpr int ADAM_TILE = 4096;  // elements per tile: 256 threads x 4 float4
+constexpr int ADAM_VECS = 2;                           // 4-element vectors per thread and stream in a tile
+constexpr int ADAM_TILE = ADAM_THREADS * 4 * ADAM_VECS;  // elements per tile: 2048
 
 // ---------------------------------------------------------------- Muon
 constexpr int TM_XK0 = 0;   // X ping buffer, K-major box {64, 128}
@@ -47,6 +48,7 @@ constexpr int TM_X1_ST = 9;
 constexpr int TMAPS_PER_MAT = 10;
 
 constexpr int PREP_TILE = 64;  // prep works on 64x64 tiles of the parameter
+constexpr int PREP_PARTIALS_PER_TILE = 8;  // one partial sum of squares per prep warp
 
 struct MatDesc {
   void* p;               // parameter, rows x cols, row-major: float32, or bf16 for dtype 1
@@ -64,7 +66,7 @@ struct MatDesc {
   int32_t prep_begin;    // first prep tile of this matrix
   int32_t prep_tiles_c;  // prep tiles along cols
   int32_t prep_count;    // number of prep tiles
-  uint32_t done;         // prep tiles finished this step (reset by the last one)
+  uint32_t done;         // unused (kept for the layout)
   int32_t tmap_base;     // index of this matrix's first tensor map
   int32_t vec;           // 4-element vectors legal for p, g, mom (and shadow) on every row
   int32_t dtype;         // MAD_DTYPE_*: 0 float32, 1 bf16, 2 float32 master + bf16 grad/shadow

@@ -153,9 +153,9 @@ def run_muon_plan(plan: MuonPlan, *, beta, nesterov, a, b, c, ns_steps, eps, lr,
         _lib.check(lib.mad_ns_gram(info, tab, it, st), "mad_ns_gram")
         timer.mark("poly")
         _lib.check(lib.mad_ns_poly(info, tab, it, b, c, st), "mad_ns_poly")
-        timer.mark("update")
-        _lib.check(lib.mad_ns_update(info, tab, it, 1 if it == ns_steps - 1 else 0, a, lr, weight_decay, st),
-                   "mad_ns_update")
+        last = it == ns_steps - 1
+        timer.mark("update_last" if last else "update")
+        _lib.check(lib.mad_ns_update(info, tab, it, 1 if last else 0, a, lr, weight_decay, st), "mad_ns_update")
     timer.mark(None)
 
 
