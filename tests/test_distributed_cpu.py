@@ -231,6 +231,21 @@ def _worker(rank, world, port, mode, q):
         sd2 = opt.state_dict()
         assert torch.equal(sd2["adam"]["state"][0]["exp_avg"], sd["adam"]["state"][0]["exp_avg"])
         assert torch.equal(sd2["muon"]["state"][3]["momentum_buffer"], sd["muon"]["state"][3]["momentum_buffer"])
+        # Gathered to one rank in host memory, then scattered back from it (the others pass None).
+        sd0 = opt.state_dict(to_rank=0, cpu=True)
+        if rank != 0:
+            assert sd0 == {}
+        opt.exp_avg.zero_()
+        opt.exp_avg_sq.zero_()
+        for t in opt.mom_segs + list(opt.master_segs):
+            t.zero_()
+        opt.load_state_dict(sd0 if rank == 0 else None, from_rank=0)
+        sd5 = opt.state_dict()
+        for br in ("adam", "muon"):
+            assert sorted(sd5[br]["state"]) == sorted(sd[br]["state"])
+            for i, st in sd[br]["state"].items():
+                for name, t in st.items():
+                    assert torch.equal(sd5[br]["state"][i][name], t), (br, i, name)
         if master:
             # A dict without masters (PyTorchMuonAdamW's layout) after the model's parameters changed: the
             # masters restart from the current bf16 parameters, and the next step continues from them.

@@ -14,7 +14,9 @@ versa.  For compatibility with the reference's ``load_state_dict``
 branch's parameter list (new parameters get zero state).
 
 In sharded (multi-GPU) mode the state lives in per-rank shards; saving
-gathers full tensors on every rank and loading scatters them back.
+gathers them one flat buffer at a time (to every rank, or to one rank and
+optionally into host memory) and loading cuts them back into shards (from a
+dict every rank holds, or scattered from one rank).
 """
 
 from __future__ import annotations
@@ -35,8 +37,6 @@ def _muon_group(mu, n):
 
 
 def branch_state_dicts(opt) -> dict:
-    if opt.distributed is not None:
-        return opt.distributed.state_dict()
     ad, mu = opt.adamw, opt.muon
     adam_state = {}
     if ad.step_num > 0:
@@ -70,9 +70,6 @@ def _replace_params(branch, params, states):
 
 @torch.no_grad()
 def load_branch_state_dicts(opt, sd: dict) -> None:
-    if opt.distributed is not None:
-        opt.distributed.load_state_dict(sd)
-        return
     ad, mu = opt.adamw, opt.muon
     if "adam" in sd:
         a = sd["adam"]

@@ -619,50 +619,93 @@ class ShardedMuonAdamW:
         return self.backend.status() if hasattr(self.backend, "status") else 0
 
     # ------------------------------------------------------------------ checkpoint
+    def _global(self, group_rank: int) -> int:
+        return dist.get_global_rank(self.pg, group_rank) if self.pg is not None else group_rank
+
+    def _gather_flat(self, shard: torch.Tensor, to_rank, cpu: bool):
+        """Every rank's ``shard`` end to end in rank order: on every rank (``to_rank`` None) or on
+        ``to_rank`` alone (None elsewhere); in host memory when ``cpu``.  One such flat at a time is
+        ever held in device memory."""
+        full = None
+        if to_rank is None:
+            full = torch.empty(shard.numel() * self.world, dtype=shard.dtype, device=shard.device)
+            dist.all_gather_into_tensor(full, shard, group=self.pg)
+        elif self.rank == to_rank:
+            full = torch.empty(shard.numel() * self.world, dtype=shard.dtype, device=shard.device)
+            dist.gather(shard, gather_list=list(full.chunk(self.world)), dst=self._global(to_rank), group=self.pg)
+        else:
+            dist.gather(shard, gather_list=None, dst=self._global(to_rank), group=self.pg)
+        if full is not None and cpu:
+            full = full.cpu()
+        return full
+
+    def _scatter_flat(self, full, shard: torch.Tensor, from_rank: int) -> None:
+        """``full`` (on ``from_rank``: every rank's shard end to end) cut into the ranks' shards."""
+        src = self._global(from_rank)
+        if self.rank == from_rank:
+            full = full.to(device=shard.device, dtype=shard.dtype)
+            dist.scatter(shard, scatter_list=list(full.chunk(self.world)), src=src, group=self.pg)
+        else:
+            dist.scatter(shard, scatter_list=None, src=src, group=self.pg)
+
     @torch.no_grad()
-    def state_dict(self):
-        """Full (gathered) state in the layout of PyTorchMuonAdamW.state_dict(); collective."""
+    def state_dict(self, to_rank=None, cpu: bool = False):
+        """Full state in the layout of ``PyTorchMuonAdamW.state_dict()``; collective.
+
+        The shards are gathered one flat buffer at a time (the AdamW moments, then each bucket's Muon
+        momentum and masters).  ``to_rank``: only that rank receives the dict (the others get ``{}``),
+        by NCCL gathers rather than all-gathers.  ``cpu``: every gathered flat goes to host memory
+        before the next one is gathered, so device memory holds one flat at most -- for large models
+        (the 8B set's state is ~36 GB) use ``state_dict(to_rank=0, cpu=True)``.  The per-parameter
+        tensors are views into those flats.
+        """
         from .checkpoint import _adam_group, _muon_group  # noqa: PLC0415
         ad, mu = self.adamw, self.muon
-        full_m = torch.empty(self.adam_shard * self.world, dtype=torch.float32, device=self.device)
-        full_v = torch.empty_like(full_m)
-        dist.all_gather_into_tensor(full_m, self.exp_avg, group=self.pg)
-        dist.all_gather_into_tensor(full_v, self.exp_avg_sq, group=self.pg)
-        full_master = None
-        if self.master_weights:
-            full_master = torch.empty_like(full_m)
-            dist.all_gather_into_tensor(full_master, self.adam_master, group=self.pg)
+        mine = to_rank is None or self.rank == to_rank
+        full_m = self._gather_flat(self.exp_avg, to_rank, cpu)
+        full_v = self._gather_flat(self.exp_avg_sq, to_rank, cpu)
+        full_master = self._gather_flat(self.adam_master, to_rank, cpu) if self.master_weights else None
         adam_state = {}
-        if ad.step_num > 0:
+        if mine and ad.step_num > 0:
             for i, p in enumerate(ad.model_params):
                 o, n = self.adam_offsets[i], self.adam_numels[i]
-                adam_state[i] = {"step": torch.tensor(float(ad.step_num), dtype=torch.float32, device=p.device),
-                                 "exp_avg": full_m[o:o + n].view_as(p).clone(),
-                                 "exp_avg_sq": full_v[o:o + n].view_as(p).clone()}
+                adam_state[i] = {"step": torch.tensor(float(ad.step_num), dtype=torch.float32,
+                                                      device="cpu" if cpu else p.device),
+                                 "exp_avg": full_m[o:o + n].view(p.shape),
+                                 "exp_avg_sq": full_v[o:o + n].view(p.shape)}
                 if full_master is not None:
-                    adam_state[i]["master_param"] = full_master[o:o + n].view_as(p).clone()
-
-        def gather(parts):
-            out = []
-            for seg, t in zip(self.seg_sizes, parts):
-                f = torch.empty(seg * self.world, dtype=t.dtype, device=self.device)
-                dist.all_gather_into_tensor(f, t, group=self.pg)
-                out.append(f)
-            return out
-
-        fulls = gather(self.mom_segs)
-        muon_state = {i: {"momentum_buffer": fulls[s.bucket][s.offset:s.offset + s.numel].view_as(p).clone()}
-                      for i, (p, s) in enumerate(zip(mu.model_params, self.slots))}
-        if self.master_weights:
-            masters = gather(self.master_segs)
+                    adam_state[i]["master_param"] = full_master[o:o + n].view(p.shape)
+        del full_m, full_v, full_master
+        muon_state = {}
+        for b, seg in enumerate(self.seg_sizes):
+            mom = self._gather_flat(self.mom_segs[b], to_rank, cpu)
+            master = self._gather_flat(self.master_segs[b], to_rank, cpu) if self.master_weights else None
+            if not mine:
+                continue
             for i, (p, s) in enumerate(zip(mu.model_params, self.slots)):
-                muon_state[i]["master_param"] = masters[s.bucket][s.offset:s.offset + s.numel].view_as(p).clone()
+                if s.bucket != b:
+                    continue
+                muon_state[i] = {"momentum_buffer": mom[s.offset:s.offset + s.numel].view(p.shape)}
+                if master is not None:
+                    muon_state[i]["master_param"] = master[s.offset:s.offset + s.numel].view(p.shape)
+        if not mine:
+            return {}
         return {"adam": {"state": adam_state, "param_groups": [_adam_group(ad, len(ad.model_params))]},
-                "muon": {"state": muon_state, "param_groups": [_muon_group(mu, len(mu.model_params))]}}
+                "muon": {"state": dict(sorted(muon_state.items())),
+                         "param_groups": [_muon_group(mu, len(mu.model_params))]}}
 
     @torch.no_grad()
-    def load_state_dict(self, sd):
-        """Load a full state dict (every rank passes the same one); each rank keeps its shard."""
+    def load_state_dict(self, sd, from_rank=None):
+        """Load a full state dict; each rank keeps its shard.
+
+        ``from_rank`` None: every rank passes the same dict.  ``from_rank=k``: only rank k holds it (the
+        others pass anything, e.g. None); the hyperparameters are broadcast and every flat is assembled on
+        rank k and scattered, one at a time.  In that form a parameter missing from the dict starts from
+        zero state (as ``torch.optim`` does), and a missing ``master_param`` from the current parameter.
+        """
+        if from_rank is not None:
+            self._load_scattered(sd, from_rank)
+            return
         ad, mu = self.adamw, self.muon
         if "adam" in sd:
             a = sd["adam"]
@@ -685,12 +728,7 @@ class ShardedMuonAdamW:
             ad.step_num = max(steps) if steps else 0
         if "muon" in sd:
             m = sd["muon"]
-            g = m["param_groups"][0]
-            mu.lr, mu.weight_decay, mu.beta, mu.is_nesterov = g["lr"], g["weight_decay"], g["momentum"], g["nesterov"]
-            if "ns_coefficients" in g:
-                mu.a, mu.b, mu.c = g["ns_coefficients"]
-            mu.eps, mu.steps = g.get("eps", mu.eps), g.get("ns_steps", mu.steps)
-            mu.adjust_lr_fn = g.get("adjust_lr_fn") or "original"
+            self._muon_hyper(m["param_groups"][0])
             for i, (p, s) in enumerate(zip(mu.model_params, self.slots)):
                 if p not in mu.momentum:        # owned by another rank
                     continue
@@ -701,6 +739,69 @@ class ShardedMuonAdamW:
                     src = st["master_param"] if st is not None and "master_param" in st else p.detach()
                     o = s.offset - self.rank * self.seg_sizes[s.bucket]
                     self.master_segs[s.bucket][o:o + s.numel].copy_(src.reshape(-1))
+
+    def _muon_hyper(self, g):
+        mu = self.muon
+        mu.lr, mu.weight_decay, mu.beta, mu.is_nesterov = g["lr"], g["weight_decay"], g["momentum"], g["nesterov"]
+        if "ns_coefficients" in g:
+            mu.a, mu.b, mu.c = g["ns_coefficients"]
+        mu.eps, mu.steps = g.get("eps", mu.eps), g.get("ns_steps", mu.steps)
+        mu.adjust_lr_fn = g.get("adjust_lr_fn") or "original"
+
+    def _load_scattered(self, sd, from_rank: int) -> None:
+        ad, mu = self.adamw, self.muon
+        root = self.rank == from_rank
+        head = [None]
+        if root:
+            a, m = sd.get("adam"), sd.get("muon")
+            steps = [int(float(st["step"])) for st in a["state"].values()] if a else []
+            head = [{"adam_group": a["param_groups"][0] if a else None,
+                     "muon_group": m["param_groups"][0] if m else None,
+                     "step": max(steps) if steps else 0}]
+        dist.broadcast_object_list(head, src=self._global(from_rank), group=self.pg)
+        head = head[0]
+        if head["adam_group"] is not None:
+            g = head["adam_group"]
+            ad.lr, (ad.beta1, ad.beta2), ad.eps, ad.weight_decay = g["lr"], tuple(g["betas"]), g["eps"], g["weight_decay"]
+            ad.step_num = head["step"]
+
+            def adam_flat(key, fallback_param=False):
+                if not root:
+                    return None
+                full = torch.zeros(self.adam_shard * self.world, dtype=torch.float32, device=self.device)
+                for i, p in enumerate(ad.model_params):
+                    st = sd["adam"]["state"].get(i)
+                    o, n = self.adam_offsets[i], self.adam_numels[i]
+                    if st is not None and key in st:
+                        full[o:o + n].copy_(st[key].reshape(-1))
+                    elif fallback_param:
+                        full[o:o + n].copy_(p.detach().reshape(-1))
+                return full
+
+            self._scatter_flat(adam_flat("exp_avg"), self.exp_avg, from_rank)
+            self._scatter_flat(adam_flat("exp_avg_sq"), self.exp_avg_sq, from_rank)
+            if self.master_weights:
+                self._scatter_flat(adam_flat("master_param", True), self.adam_master, from_rank)
+        if head["muon_group"] is not None:
+            self._muon_hyper(head["muon_group"])
+            for b, seg in enumerate(self.seg_sizes):
+                def muon_flat(key, dtype, fallback_param=False):
+                    if not root:
+                        return None
+                    full = torch.zeros(seg * self.world, dtype=dtype, device=self.device)
+                    for i, (p, s) in enumerate(zip(mu.model_params, self.slots)):
+                        if s.bucket != b:
+                            continue
+                        st = sd["muon"]["state"].get(i)
+                        if st is not None and key in st:
+                            full[s.offset:s.offset + s.numel].copy_(st[key].reshape(-1))
+                        elif fallback_param:
+                            full[s.offset:s.offset + s.numel].copy_(p.detach().reshape(-1))
+                    return full
+
+                self._scatter_flat(muon_flat("momentum_buffer", self.mom_segs[b].dtype), self.mom_segs[b], from_rank)
+                if self.master_weights:
+                    self._scatter_flat(muon_flat("master_param", torch.float32, True), self.master_segs[b], from_rank)
 
 
 __all__ = ["ShardedMuonAdamW", "CudaBackend", "lpt_assign", "split_buckets", "muon_layout", "zero1_layout",

@@ -313,7 +313,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         return st
 
     # -- checkpointing -----------------------------------------------------
-    def state_dict(self) -> dict[str, object]:
+    def state_dict(self, to_rank: int | None = None, cpu: bool = False) -> dict[str, object]:
         """Optimizer state in the layout of ``PyTorchMuonAdamW.state_dict()``.
 
         ``{"adam": <torch.optim.AdamW state dict>, "muon": <torch.optim.Muon
@@ -321,13 +321,32 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         ``momentum_buffer``, indexed by position in each branch's parameter
         list, so checkpoints move between the two classes.  (The reference's
         own ``state_dict`` returns only the parameter lists, optimizer.py:166-168.)
+
+        Sharded (collective): the shards are gathered one flat buffer at a
+        time; ``to_rank=k`` delivers the dict to rank k only (``{}``
+        elsewhere) and ``cpu=True`` moves each gathered buffer to host memory
+        before the next, so device memory never holds more than one.  On one
+        GPU ``cpu=True`` returns host copies and ``to_rank`` has no effect.
         """
         from .checkpoint import branch_state_dicts  # noqa: PLC0415
-        return branch_state_dicts(self)
+        if self.distributed is not None:
+            return self.distributed.state_dict(to_rank=to_rank, cpu=cpu)
+        sd = branch_state_dicts(self)
+        if cpu:
+            sd = {k: {"state": {i: {n: t.detach().cpu() for n, t in st.items()} for i, st in br["state"].items()},
+                      "param_groups": br["param_groups"]} for k, br in sd.items()}
+        return sd
 
-    def load_state_dict(self, state_dict: dict[str, object]) -> None:
-        """Load a dict produced by :meth:`state_dict` or by ``PyTorchMuonAdamW.state_dict()``."""
+    def load_state_dict(self, state_dict: dict[str, object], from_rank: int | None = None) -> None:
+        """Load a dict produced by :meth:`state_dict` or by ``PyTorchMuonAdamW.state_dict()``.
+
+        Sharded (collective): with ``from_rank=k`` only rank k needs the dict
+        (the others may pass ``None``); it is scattered one buffer at a time.
+        """
         from .checkpoint import load_branch_state_dicts  # noqa: PLC0415
+        if self.distributed is not None:
+            self.distributed.load_state_dict(state_dict, from_rank=from_rank)
+            return
         load_branch_state_dicts(self, state_dict)
 
 
