@@ -9,14 +9,14 @@
 // with every product and sum rounded separately (no FMA contraction) so it
 // agrees with the float32 CPU oracle to the last few ulps.
 //
-// Layout: a multi-tensor launch walks a table of tensors cut into 4096-element
-// tiles; a tile -> tensor index map (int32 per tile) sits in front of the
-// AdamEntry array, so each CTA finds its tensor with one load (and loads the
-// next tile's entry while it works on the current one).  Each thread moves
-// ADAM_VECS float4 of each of p, g, m, v per tile; many small resident CTAs
-// (four per SM) keep the bytes in flight the HBM3e streaming roofline needs
-// -- 28 bytes per element -- and the warps to cover the division and
-// square-root chains at the power-capped SM clock.
+// Layout: a multi-tensor launch covers a table of tensors cut into 512-element
+// tiles, one tile per 128-thread CTA; a tile -> tensor index map (int32 per
+// tile) sits in front of the AdamEntry array, so each CTA finds its tensor
+// with one load.  Each thread moves one float4 of each of p, g, m, v.  The
+// grid is the tile count: the hardware keeps up to sixteen such CTAs per SM
+// resident, and that occupancy -- not a deep per-thread pipeline -- is what
+// keeps the 28 bytes per element streaming at the power-capped SM clock of
+// the optimizer step.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -186,38 +186,21 @@ __device__ __forceinline__ void adam_tile_any(const AdamEntry& e, int64_t off, i
 
 // REDUCE: the gradient summed over ranks (a separate instantiation, so the
 // local path keeps its register budget and occupancy).
-constexpr int ADAM_CTAS_PER_SM = 4;         // resident CTAs of the local-gradient kernel
-constexpr int ADAM_REDUCE_CTAS_PER_SM = 1;  // the rank-summing kernel's registers allow one
-
-__device__ __forceinline__ void prefetch_l1(const void* p) {
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)) : "memory");
-}
-
-// The next tile's table entry (two dependent loads: tile map, then entry) is
-// requested while the current tile is processed -- its index into a register,
-// its 64-byte entry into L1 -- so a CTA's data loads for a tile go out as soon
-// as it starts the tile.
+// One tile per CTA (the grid covers every tile).  REDUCE: the gradient summed
+// over ranks (a separate instantiation with its own register budget).
 template <bool REDUCE>
-__global__ void __launch_bounds__(ADAM_THREADS, REDUCE ? ADAM_REDUCE_CTAS_PER_SM : ADAM_CTAS_PER_SM)
-    adamw_multi_kernel(const AdamEntry* __restrict__ entries, const int32_t* __restrict__ tile_map, int64_t n_tiles,
-                       AdamScalars s) {
-  int64_t tile = blockIdx.x;
+__global__ void __launch_bounds__(ADAM_THREADS, REDUCE ? 4 : 8) adamw_multi_kernel(
+    const AdamEntry* __restrict__ entries, const int32_t* __restrict__ tile_map, int64_t n_tiles, AdamScalars s) {
+  const int64_t tile = blockIdx.x;
   if (tile >= n_tiles) return;
-  int32_t idx = tile_map[tile];
-  for (; tile < n_tiles; tile += gridDim.x) {
-    const AdamEntry e = entries[idx];
-    const int64_t next = tile + gridDim.x;
-    const int32_t next_idx = next < n_tiles ? __ldg(tile_map + next) : idx;
-    const int64_t off = (tile - e.tile_begin) * ADAM_TILE;
-    const int64_t rem = e.numel - off;
-    const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
-    adam_tile_any<REDUCE>(e, off, len, s);
-    if (threadIdx.x == 0) prefetch_l1(entries + next_idx);
-    idx = next_idx;
-  }
+  const AdamEntry& e = entries[tile_map[tile]];
+  const int64_t off = (tile - e.tile_begin) * ADAM_TILE;
+  const int64_t rem = e.numel - off;
+  const int len = static_cast<int>(rem < ADAM_TILE ? rem : ADAM_TILE);
+  adam_tile_any<REDUCE>(e, off, len, s);
 }
 
-__global__ void __launch_bounds__(ADAM_THREADS, ADAM_CTAS_PER_SM) adamw_single_kernel(AdamEntry e, int64_t n_tiles, AdamScalars s) {
+__global__ void __launch_bounds__(ADAM_THREADS, 12) adamw_single_kernel(AdamEntry e, int64_t n_tiles, AdamScalars s) {
   for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
     const int64_t off = tile * ADAM_TILE;
     const int64_t rem = e.numel - off;
@@ -244,10 +227,10 @@ static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, f
   return s;
 }
 
-static int adam_grid(int64_t n_tiles, int per_sm) {
-  // per_sm resident CTAs of 256 threads per SM, striding over the tiles.
-  const int64_t cap = static_cast<int64_t>(num_sms()) * per_sm;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n_tiles, cap)));
+static int adam_grid(int64_t n_tiles) {
+  // One CTA per tile.  A plan never has more than 2^31 - 1 tiles (mad_adamw_plan
+  // refuses more); the single-tensor kernel strides over any beyond the cap.
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n_tiles, INT32_MAX)));
 }
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -296,7 +279,7 @@ extern "C" int mad_adamw_step(float* param, const float* grad, float* exp_avg, f
   e.dtype = MAD_DTYPE_F32;
   e.vec = vec_ok(param, grad, exp_avg, exp_avg_sq, nullptr, MAD_DTYPE_F32);
   const int64_t n_tiles = (numel + ADAM_TILE - 1) / ADAM_TILE;
-  adamw_single_kernel<<<adam_grid(n_tiles, ADAM_CTAS_PER_SM), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+  adamw_single_kernel<<<adam_grid(n_tiles), ADAM_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       e, n_tiles, make_scalars(lr, beta1, beta2, eps, weight_decay, bias1, bias2));
   return check_launch("adamw_single_kernel");
 }
@@ -378,11 +361,9 @@ static int adamw_step_multi(const void* dev_table, int64_t n_tiles, float lr, fl
   const AdamEntry* entries = reinterpret_cast<const AdamEntry*>(base + entries_offset(n_tiles));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (sc.red.n > 0)
-    adamw_multi_kernel<true><<<adam_grid(n_tiles, ADAM_REDUCE_CTAS_PER_SM), ADAM_THREADS, 0, st>>>(entries, tile_map,
-                                                                                                 n_tiles, sc);
+    adamw_multi_kernel<true><<<adam_grid(n_tiles), ADAM_THREADS, 0, st>>>(entries, tile_map, n_tiles, sc);
   else
-    adamw_multi_kernel<false><<<adam_grid(n_tiles, ADAM_CTAS_PER_SM), ADAM_THREADS, 0, st>>>(entries, tile_map,
-                                                                                           n_tiles, sc);
+    adamw_multi_kernel<false><<<adam_grid(n_tiles), ADAM_THREADS, 0, st>>>(entries, tile_map, n_tiles, sc);
   return check_launch("adamw_multi_kernel");
 }
 

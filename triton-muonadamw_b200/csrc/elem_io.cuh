@@ -143,41 +143,3 @@ __device__ __forceinline__ float ld1_ranks(const T* g, int64_t i, const GradRedu
 }
 
 }  // namespace mad
-
-namespace mad {
-
-// ------------------------------------------------------------ cp.async staging
-// Asynchronous global -> shared copies (LDGSTS) for the streaming kernels:
-// the bytes in flight live in shared memory instead of registers, so a CTA
-// can keep several tiles of loads outstanding.  Each thread copies, and
-// later reads, only its own slots, so completion is tracked per thread with
-// commit/wait groups and no block-wide barrier is needed.
-__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gptr) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr) : "memory");
-}
-__device__ __forceinline__ void cp_async8(uint32_t smem_addr, const void* gptr) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr), "l"(gptr) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// Wait until at most N of this thread's committed groups are still pending.
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ uint32_t smem_addr_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// A 4-element vector of T (16 B float32, 8 B bf16) copied into a 16-byte slot.
-__device__ __forceinline__ void cp_async_vec(uint32_t slot, const float* g) { cp_async16(slot, g); }
-__device__ __forceinline__ void cp_async_vec(uint32_t slot, const __nv_bfloat16* g) { cp_async8(slot, g); }
-
-// The slot read back and widened to float32.
-__device__ __forceinline__ float4 slot_vec(const float4* slot, const float*) { return *slot; }
-__device__ __forceinline__ float4 slot_vec(const float4* slot, const __nv_bfloat16*) {
-  const uint2 u = *reinterpret_cast<const uint2*>(slot);
-  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
-                     __uint_as_float(u.y & 0xFFFF0000u));
-}
-
-}  // namespace mad

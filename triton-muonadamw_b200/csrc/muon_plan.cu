@@ -116,6 +116,27 @@ int encode_bf16(CUtensorMap* out, void* base, int64_t rows, int64_t cols, int64_
   return MAD_OK;
 }
 
+// A parameter (rows x cols, float32 or bf16) in 32x32 boxes for the last
+// update's TMA loads and stores: 128-byte rows of float32 take the 128-byte
+// swizzle, 64-byte rows of bf16 the 64-byte one.  Returns false (and leaves
+// the map unused) when TMA cannot address the tensor: a base that is not
+// 16-byte aligned or a row pitch that is not a multiple of 16 bytes.
+bool encode_param(CUtensorMap* out, void* base, int64_t rows, int64_t cols, bool f32) {
+  const int64_t pitch = cols * (f32 ? 4 : 2);
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (pitch & 15) || rows > (int64_t(1) << 31) ||
+      cols > (int64_t(1) << 31))
+    return false;
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(out, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int validate(const mad_muon_matrix* mats, int32_t n) {
   if (n < 0 || (n > 0 && !mats)) return fail(MAD_ERR_INVALID, "muon plan: bad matrix list");
   for (int32_t i = 0; i < n; ++i) {
@@ -245,6 +266,10 @@ extern "C" int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* 
     if (int rc = encode_bf16(t + TM_POLY_ST, d.poly, s.m, s.m, s.ld_mm, 32, 32)) return rc;
     if (int rc = encode_bf16(t + TM_X0_ST, d.x[0], s.m, s.n, s.ld_x, 32, 32)) return rc;
     if (int rc = encode_bf16(t + TM_X1_ST, d.x[1], s.m, s.n, s.ld_x, 32, 32)) return rc;
+    // The parameter as stored (rows x cols), for the last update's writes.
+    d.p_tma = encode_param(t + TM_P, mt.param, mt.rows, mt.cols, mt.dtype != MAD_DTYPE_BF16) ? 1 : 0;
+    if (d.p_tma && mt.dtype == MAD_DTYPE_F32_MASTER)
+      d.p_tma = encode_param(t + TM_SH, mt.shadow, mt.rows, mt.cols, false) ? 1 : 0;
     if (buffers) {
       mad_muon_buffers& b = buffers[i];
       b.x[0] = d.x[0];

@@ -7,21 +7,20 @@
 // epilogues.
 //
 // The pass is HBM-bound: 14 B per element with float32 buffers (read g, mom;
-// write mom, X), 8 B with bf16 buffers.  To keep bytes in flight at the
-// power-capped SM clock the loop never stalls a CTA on bookkeeping:
-//  * each warp writes the sum of squares of its part of a 64x64 tile to its
-//    own slot (no block-wide reduction, no atomics, no fences in the loop);
-//    a second launch, one CTA per matrix, adds a matrix's slots in a fixed
-//    order in double precision -- the norm is deterministic;
-//  * the gradient and momentum of a CTA's next two tiles are copied into a
-//    shared-memory ring (cp.async) while the current tile is computed and
-//    stored: two tiles of loads in flight per CTA, four per SM, held in
-//    shared memory rather than registers;
+// write mom, X), 8 B with bf16 buffers.  It runs in the optimizer step at the
+// SM clock the power-capped Newton-Schulz GEMMs leave, where resident warps,
+// not per-thread pipelining, keep the bytes in flight:
+//  * one 64x64 tile per 256-thread CTA over a grid of every tile, four CTAs
+//    per SM, all of a tile's loads issued before its arithmetic;
+//  * each warp writes the sum of squares of its part of the tile to its own
+//    slot (no block-wide reduction, no atomics, no fences); a second launch,
+//    one CTA per matrix, adds a matrix's slots in a fixed order in double
+//    precision -- the norm is deterministic;
 //  * tall matrices are transposed through a bf16 shared-memory tile (the
-//    only block barriers of the loop).
+//    kernel's only block barriers).
 // With a gradient reduction the other ranks' gradient copies are read over
-// NVLink instead (a separate kernel that reads directly: its summed loads
-// keep two ranks' vectors in flight per thread).
+// NVLink as well (its own instantiation: the summed loads keep two ranks'
+// vectors in flight per thread).
 #include <cuda_runtime.h>
 
 #include "capi_common.h"
@@ -35,6 +34,7 @@ constexpr int PREP_THREADS = 256;
 constexpr int PREP_WARPS = PREP_THREADS / 32;  // partial sums per tile (one per warp)
 static_assert(PREP_WARPS == PREP_PARTIALS_PER_TILE, "plan layout of the partial sums");
 constexpr int FINALIZE_THREADS = 512;
+constexpr int PREP_T_PITCH = PREP_TILE + 2;  // bf16 transpose tile row pitch (132 B: 4-byte reads, 2-way writes)
 
 struct PrepScalars {
   float beta, one_m_beta, eps_bf16;
@@ -164,7 +164,7 @@ __device__ __forceinline__ uint32_t pack2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
 // bf16 cast of u, this thread's sum of squares, and the X store (direct, or
 // through shared memory for tall matrices).
 __device__ __forceinline__ void write_x(const TileRef2& tr, const float (&xv)[4][4], float& ss,
-                                        __nv_bfloat16 (*tile_t)[PREP_TILE + 2]) {
+                                        __nv_bfloat16 (*tile_t)[PREP_T_PITCH]) {
   const MatDesc* md = tr.md;
   const int t = threadIdx.x, rows = md->rows, cols = md->cols, ld_x = md->ld_x;
   const int cl = (t & 15) * 4;
@@ -220,132 +220,55 @@ __device__ __forceinline__ void write_x(const TileRef2& tr, const float (&xv)[4]
   __syncthreads();  // every thread has read the tile before the next one is written
 }
 
-// ---------------------------------------------------------------- local gradients: cp.async ring
-// Each CTA strides over the tiles; the gradient and momentum of its tile
-// k + PREP_STAGES - 1 are copied into shared memory (cp.async, one 16-byte
-// slot per thread, row and array) while tile k is computed, so PREP_STAGES - 1
-// tiles of loads stay in flight per CTA without holding registers.  A thread
-// reads back only the slots it copied: no barrier guards the ring.
-constexpr int PREP_STAGES = 3;
-constexpr int PREP_SLOTS = 8;  // per thread and tile: 4 rows x (gradient, momentum)
-constexpr int PREP_STAGE_BYTES = PREP_SLOTS * PREP_THREADS * 16;
-constexpr int PREP_T_PITCH = PREP_TILE + 2;  // bf16 transpose tile row pitch (132 B: 4-byte reads, 2-way writes)
-constexpr int PREP_SMEM_BYTES = PREP_STAGES * PREP_STAGE_BYTES + PREP_TILE * PREP_T_PITCH * 2;
-
+// ---------------------------------------------------------------- the prep kernel
 template <typename TM, typename TG>
-__device__ __forceinline__ void issue_tile_typed(const TileRef2& tr, float4* stage) {
-  const TG* g = static_cast<const TG*>(tr.md->g);
-  const TM* mom = static_cast<const TM*>(tr.md->mom);
-  const int t = threadIdx.x;
+__device__ __forceinline__ void load_full_typed(const TileRef2& tr, TileRegs& r) {
+  const TG* __restrict__ g = static_cast<const TG*>(tr.md->g);
+  const TM* __restrict__ mom = static_cast<const TM*>(tr.md->mom);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t off = vec_offset(tr, i);
-    cp_async_vec(smem_addr_u32(stage + i * PREP_THREADS + t), g + off);
-    cp_async_vec(smem_addr_u32(stage + (4 + i) * PREP_THREADS + t), mom + off);
+    r.g[i] = ld4(g + off, 0);
+    r.m[i] = ld4(mom + off, 0);
   }
 }
 
-// Copies of one full tile into a ring stage, then one commit group (empty for
-// tiles the general path handles, so the group count stays uniform).
-__device__ __forceinline__ void issue_tile(const TileRef2& tr, bool valid, float4* stage) {
-  if (valid && tr.full) {
-    if (tr.md->dtype == MAD_DTYPE_BF16)
-      issue_tile_typed<__nv_bfloat16, __nv_bfloat16>(tr, stage);
-    else if (tr.md->dtype == MAD_DTYPE_F32_MASTER)
-      issue_tile_typed<float, __nv_bfloat16>(tr, stage);
-    else
-      issue_tile_typed<float, float>(tr, stage);
-  }
-  cp_async_commit();
-}
-
-template <typename TM, typename TG>
-__device__ __forceinline__ void read_tile_typed(const float4* stage, TileRegs& r) {
-  const int t = threadIdx.x;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    r.g[i] = slot_vec(stage + i * PREP_THREADS + t, static_cast<const TG*>(nullptr));
-    r.m[i] = slot_vec(stage + (4 + i) * PREP_THREADS + t, static_cast<const TM*>(nullptr));
-  }
-}
-
-__global__ void __launch_bounds__(PREP_THREADS, 2) muon_prep_ring_kernel(MatDesc* __restrict__ mats,
-                                                                          const int32_t* __restrict__ prep_map,
-                                                                          float* __restrict__ partials,
-                                                                          int64_t n_tiles, PrepScalars s) {
-  extern __shared__ __align__(16) uint8_t prep_smem[];
-  float4* ring = reinterpret_cast<float4*>(prep_smem);
-  auto tile_t = reinterpret_cast<__nv_bfloat16 (*)[PREP_T_PITCH]>(prep_smem + PREP_STAGES * PREP_STAGE_BYTES);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t G = gridDim.x;
-  int64_t tile = blockIdx.x;
-  if (tile >= n_tiles) return;
-
-  // Tiles k, k+1, k+2 of this CTA: a (being computed), b, c (in flight).
-  TileRef2 a = locate(mats, prep_map, tile);
-  TileRef2 b = a;
-  const bool b_ok = tile + G < n_tiles;
-  if (b_ok) b = locate(mats, prep_map, tile + G);
-  issue_tile(a, true, ring);
-  issue_tile(b, b_ok, ring + PREP_SLOTS * PREP_THREADS);
-  int st = 0;
-  for (; tile < n_tiles; tile += G) {
-    const int64_t far = tile + 2 * G;
-    TileRef2 c = b;
-    const bool c_ok = far < n_tiles;
-    if (c_ok) c = locate(mats, prep_map, far);
-    const int st_far = st == 0 ? 2 : st - 1;  // (st + 2) % 3
-    issue_tile(c, c_ok, ring + st_far * PREP_SLOTS * PREP_THREADS);
-    cp_async_wait<PREP_STAGES - 1>();  // this thread's copies of tile k have landed
-
-    float xv[4][4];
-    if (a.full) {
-      TileRegs r;
-      const float4* stage = ring + st * PREP_SLOTS * PREP_THREADS;
-      if (a.md->dtype == MAD_DTYPE_BF16) {
-        read_tile_typed<__nv_bfloat16, __nv_bfloat16>(stage, r);
-        finish_full<__nv_bfloat16>(a, r, xv, s);
-      } else if (a.md->dtype == MAD_DTYPE_F32_MASTER) {
-        read_tile_typed<float, __nv_bfloat16>(stage, r);
-        finish_full<float>(a, r, xv, s);
-      } else {
-        read_tile_typed<float, float>(stage, r);
-        finish_full<float>(a, r, xv, s);
-      }
-    } else {
-      values_general_any<false>(a, xv, s);
-    }
-    float ss = 0.f;
-    write_x(a, xv, ss, tile_t);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) partials[tile * PREP_WARPS + warp] = ss;
-    a = b;
-    b = c;
-    st = st == 2 ? 0 : st + 1;
-  }
-  cp_async_wait<0>();
-}
-
-// ---------------------------------------------------------------- gradients summed over ranks
-// Every rank's copy is read over NVLink with two ranks' vectors in flight per
-// thread (ld4_ranks_rows); those loads bound this path, so it reads directly.
-__global__ void __launch_bounds__(PREP_THREADS, 2) muon_prep_reduce_kernel(MatDesc* __restrict__ mats,
-                                                                            const int32_t* __restrict__ prep_map,
-                                                                            float* __restrict__ partials,
-                                                                            int64_t n_tiles, PrepScalars s) {
+// One 64x64 tile per CTA; the grid covers every tile and the hardware keeps
+// four CTAs per SM resident.  A full tile's loads are all issued before any
+// arithmetic.  REDUCE: the gradient summed over ranks (its own instantiation
+// and register budget).  Each warp stores its sum of squares to
+// partials[tile * PREP_WARPS + warp].
+template <bool REDUCE>
+__global__ void __launch_bounds__(PREP_THREADS, REDUCE ? 2 : 4) muon_prep_kernel(MatDesc* __restrict__ mats,
+                                                                                const int32_t* __restrict__ prep_map,
+                                                                                float* __restrict__ partials,
+                                                                                int64_t n_tiles, PrepScalars s) {
   __shared__ __nv_bfloat16 tile_t[PREP_TILE][PREP_T_PITCH];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-    const TileRef2 cur = locate(mats, prep_map, tile);
-    float xv[4][4];
-    values_general_any<true>(cur, xv, s);
-    float ss = 0.f;
-    write_x(cur, xv, ss, tile_t);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) partials[tile * PREP_WARPS + warp] = ss;
+  const int64_t tile = blockIdx.x;
+  if (tile >= n_tiles) return;
+  const TileRef2 cur = locate(mats, prep_map, tile);
+  float xv[4][4];
+  if (!REDUCE && cur.full) {
+    TileRegs r;
+    if (cur.md->dtype == MAD_DTYPE_BF16) {
+      load_full_typed<__nv_bfloat16, __nv_bfloat16>(cur, r);
+      finish_full<__nv_bfloat16>(cur, r, xv, s);
+    } else if (cur.md->dtype == MAD_DTYPE_F32_MASTER) {
+      load_full_typed<float, __nv_bfloat16>(cur, r);
+      finish_full<float>(cur, r, xv, s);
+    } else {
+      load_full_typed<float, float>(cur, r);
+      finish_full<float>(cur, r, xv, s);
+    }
+  } else {
+    values_general_any<REDUCE>(cur, xv, s);
   }
+  float ss = 0.f;
+  write_x(cur, xv, ss, tile_t);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) partials[tile * PREP_WARPS + warp] = ss;
 }
 
 // One CTA per matrix: the sum of its tiles' partial sums of squares, in a
@@ -394,20 +317,13 @@ int launch_muon_prep(MatDesc* mats, int32_t n_mats, const int32_t* prep_map, flo
   s.one_m_beta = static_cast<float>(1.0 - beta);
   s.eps_bf16 = bf16_round(eps);
   s.nesterov = nesterov ? 1 : 0;
-  // Two resident CTAs per SM (the ring's shared memory; the rank-summing
-  // kernel's registers); every CTA strides over the tiles.
-  const int64_t cap = static_cast<int64_t>(num_sms()) * 2;
-  const int grid = static_cast<int>(n_tiles < cap ? n_tiles : cap);
-  if (red.n > 0) {
-    muon_prep_reduce_kernel<<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
-    if (int rc = check_launch("muon_prep_reduce_kernel")) return rc;
-  } else {
-    if (cudaFuncSetAttribute(muon_prep_ring_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM_BYTES) !=
-        cudaSuccess)
-      return fail_cuda("cudaFuncSetAttribute(muon_prep_ring_kernel)");
-    muon_prep_ring_kernel<<<grid, PREP_THREADS, PREP_SMEM_BYTES, stream>>>(mats, prep_map, partials, n_tiles, s);
-    if (int rc = check_launch("muon_prep_ring_kernel")) return rc;
-  }
+  // One CTA per tile (a plan never has more than 2^31 - 1 prep tiles).
+  const int grid = static_cast<int>(n_tiles);
+  if (red.n > 0)
+    muon_prep_kernel<true><<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
+  else
+    muon_prep_kernel<false><<<grid, PREP_THREADS, 0, stream>>>(mats, prep_map, partials, n_tiles, s);
+  if (int rc = check_launch("muon_prep_kernel")) return rc;
   muon_norm_kernel<<<n_mats, FINALIZE_THREADS, 0, stream>>>(mats, partials, s.eps_bf16);
   return check_launch("muon_norm_kernel");
 }

@@ -39,7 +39,7 @@
 namespace mad {
 namespace ns {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
+constexpr int BM = 128, BN = 256, BK = 64, MAX_STAGES = 6;
 constexpr int PAIR_M = 2 * BM;          // rows of a pair tile
 constexpr int A_BYTES = BM * BK * 2;    // 16 KB: this CTA's 128 rows of A
 constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB: this CTA's 128 columns of B
@@ -49,12 +49,22 @@ constexpr int TMEM_COLS = 2 * BN;
 constexpr int EPI_WARPS = 8;
 constexpr int EPI_THREADS = EPI_WARPS * 32;
 constexpr int NUM_THREADS = 64 + EPI_THREADS;  // producer warp, MMA warp, epilogue warps
-// Each epilogue warp stages its 32x32 output block (and the transposed mirror
-// block) in shared memory for a TMA store: 2 x 2 KB per warp.
-constexpr int STAGE_OUT_BYTES = 4096;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + 1024 + 1024;  // + barriers, alignment
-
 enum Mode { GRAM = 0, POLY = 1, UPDATE = 2, UPDATE_LAST = 3 };
+
+// Shared memory per mode.  Each epilogue warp has a staging area: GRAM/POLY
+// stage their 32x32 output block and its transposed mirror (2 x 2 KB), UPDATE
+// its output block and the X block of the a*X term (2 x 2 KB).  UPDATE_LAST
+// also moves the parameter block (a 32x32 box, 4 KB float32) and the bf16
+// shadow by TMA: 8 KB per warp, paid for with one ring stage fewer.
+template <int MODE>
+struct Smem {
+  static constexpr int STAGES = MODE == UPDATE_LAST ? 5 : 6;
+  static constexpr int STAGE_OUT = MODE == UPDATE_LAST ? 8192 : 4096;
+  static constexpr int BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT + 1024 + 1024;  // + barriers, alignment
+};
+static_assert(Smem<GRAM>::BYTES <= 227 * 1024 && Smem<UPDATE_LAST>::BYTES <= 227 * 1024, "shared memory per CTA");
+// Offsets inside an UPDATE_LAST warp's staging area.
+constexpr int LAST_SHADOW_OFF = 0, LAST_X_OFF = 2048, LAST_P_OFF = 4096;
 
 // UPDATE_LAST is the update of the final iteration, which writes the
 // parameters; it is a separate instantiation so the common path can keep two
@@ -130,7 +140,7 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
       } else {
         tma_load_2d_pair(sb, tmB, bar, kb * BK, bcol);
       }
-      if (++stage == STAGES) {
+      if (++stage == Smem<MODE>::STAGES) {
         stage = 0;
         phase ^= 1u;
       }
@@ -181,7 +191,7 @@ __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, ui
       const uint32_t e = smem_u32(&empty[stage]);
       tc_commit_pair(mapa_shared(e, 0));
       tc_commit_pair(mapa_shared(e, 1));
-      if (++stage == STAGES) {
+      if (++stage == Smem<MODE>::STAGES) {
         stage = 0;
         phase ^= 1u;
       }
@@ -383,41 +393,144 @@ __device__ __forceinline__ void write_params(const MatDesc& md, const float (&v)
   }
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)) : "memory");
+// ---------------------------------------------------------------- UPDATE_LAST: parameter blocks by TMA
+// The last update rewrites the parameter.  Where the plan could describe it
+// with a tensor map (MatDesc::p_tma), each epilogue warp moves its 32x32
+// parameter block for a chunk -- X' rows grow0.., columns gcol0.., i.e. the
+// box at (gcol0, grow0) of the parameter, or (grow0, gcol0) for a tall one --
+// with one TMA load into its staging area, updates it there in place, and
+// writes it back (and the bf16 shadow of a float32 master) with TMA stores:
+// no per-thread global traffic, and an evict-first L2 policy so the
+// parameter stream does not displace the B and X operands the other tiles
+// still read.  One parameter buffer per warp: the next chunk's block is
+// loaded as soon as the previous block's stores have read it.
+struct LastIo {
+  uint64_t* bar;   // this warp's parameter-load barrier
+  uint32_t phase;
+  uint32_t on;     // this tile's chunks take the TMA path
+  uint32_t failed; // a parameter-load wait gave up
+};
+
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ unsigned short ld_shared_u16(uint32_t addr) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+__device__ __forceinline__ unsigned short float_to_bf16_bits(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
-// UPDATE_LAST: pull the parameter block this warp will read and rewrite for a
-// tile -- X' rows grow0..grow0+31 x columns col0..col0+127 -- into L2 a tile
-// ahead, so the epilogue's parameter loads hit L2 instead of waiting on DRAM.
-// Only lines that hold parameter elements are touched.
-__device__ __forceinline__ void prefetch_param_block(const MatDesc& md, int grow0, int col0) {
+// TMA load of the parameter block of the chunk at X' columns gcol0.. (lane 0).
+__device__ __forceinline__ void last_p_issue(const MatDesc& md, const CUtensorMap* maps, uint8_t* stage, LastIo& io,
+                                             int grow0, int gcol0) {
+  if ((threadIdx.x & 31) == 0) {
+    bulk_wait_read_all();  // the previous block's stores have finished reading the staging area
+    mbar_arrive_expect_tx(io.bar, md.dtype == MAD_DTYPE_BF16 ? 2048u : 4096u);
+    const int x = md.transposed ? grow0 : gcol0, y = md.transposed ? gcol0 : grow0;
+    tma_load_2d_hint(stage + LAST_P_OFF, maps + TM_P, io.bar, x, y, l2_policy_evict_first());
+  }
+}
+
+// The chunk's parameter update on the staged block, then its TMA store(s).
+// Lane l owns X' row grow0 + l: parameter row grow0 + l (block row l) or, for
+// a tall parameter, parameter column grow0 + l (block column l).  Float32
+// blocks use the 128-byte swizzle (16-byte unit u of row r at r*128 +
+// 16*(u ^ (r & 7))), bf16 blocks and the shadow the 64-byte one.  Elements
+// outside the parameter are zero-filled on the load and clipped on the store.
+template <typename T, bool SHADOW>
+__device__ __forceinline__ void write_params_tma(const MatDesc& md, const CUtensorMap* maps, const float (&v)[32],
+                                                 int grow0, int gcol0, float slr, float lr_wd, uint8_t* stage,
+                                                 LastIo& io, unsigned int* status, long long limit) {
   const int lane = threadIdx.x & 31;
-  const int es = md.dtype == MAD_DTYPE_BF16 ? 2 : 4;
-  const char* base = static_cast<const char*>(md.p);
-  if (grow0 >= md.m || col0 >= md.n) return;
-  if (!md.transposed) {
-    // Parameter row grow0 + lane, columns col0 .. min(col0 + 128, n).
-    const int r = grow0 + lane;
-    if (r >= md.m) return;
-    const int cend = col0 + 128 < md.n ? col0 + 128 : md.n;
-    const uintptr_t a = reinterpret_cast<uintptr_t>(base + (static_cast<int64_t>(r) * md.n + col0) * es);
-    const uintptr_t e = reinterpret_cast<uintptr_t>(base + (static_cast<int64_t>(r) * md.n + cend) * es);
-    for (uintptr_t l = a & ~static_cast<uintptr_t>(127); l < e; l += 128) prefetch_l2(reinterpret_cast<const void*>(l));
-  } else {
-    // Parameter rows col0 .. col0+127 (four per lane), columns grow0 .. grow0+31: one line each.
+  if (!mbar_wait(io.bar, io.phase, status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE, limit)) {
+    io.failed = 1;
+    return;
+  }
+  io.phase ^= 1u;
+  const uint32_t pb = smem_u32(stage + LAST_P_OFF), sb = smem_u32(stage + LAST_SHADOW_OFF);
+  if (sizeof(T) == 4) {
+    if (!md.transposed) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int pr = col0 + 4 * lane + j;
-      if (pr < md.n) prefetch_l2(base + (static_cast<int64_t>(pr) * md.m + grow0) * es);
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t a = pb + lane * 128 + 16 * (u ^ (lane & 7));
+        uint4 q = ld_shared_v4(a);
+        float w0 = param_new<T>(__uint_as_float(q.x), v[4 * u + 0], slr, lr_wd);
+        float w1 = param_new<T>(__uint_as_float(q.y), v[4 * u + 1], slr, lr_wd);
+        float w2 = param_new<T>(__uint_as_float(q.z), v[4 * u + 2], slr, lr_wd);
+        float w3 = param_new<T>(__uint_as_float(q.w), v[4 * u + 3], slr, lr_wd);
+        q.x = __float_as_uint(w0);
+        q.y = __float_as_uint(w1);
+        q.z = __float_as_uint(w2);
+        q.w = __float_as_uint(w3);
+        st_shared_v4(a, q);
+        if (SHADOW) {
+          // bf16 columns 4u..4u+3 of shadow row `lane`: half of a 16-byte unit
+          const uint32_t sa = sb + sw64_offset(lane, u >> 1) + 8 * (u & 1);
+          asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(sa), "r"(pack_bf16x2(w0, w1)), "r"(pack_bf16x2(w2, w3))
+                       : "memory");
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const uint32_t a = pb + k * 128 + 16 * ((lane >> 2) ^ (k & 7)) + 4 * (lane & 3);
+        const float w = param_new<T>(ld_shared_f32(a), v[k], slr, lr_wd);
+        st_shared_f32(a, w);
+        if (SHADOW) st_shared_u16(sb + sw64_offset(k, lane >> 3) + 2 * (lane & 7), float_to_bf16_bits(w));
+      }
     }
+  } else {
+    if (!md.transposed) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t a = pb + sw64_offset(lane, u);
+        uint4 q = ld_shared_v4(a);
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = param_new<T>(bf16_bits_to_float(w[j] & 0xFFFFu), v[8 * u + 2 * j], slr, lr_wd);
+          const float hi = param_new<T>(bf16_bits_to_float(w[j] >> 16), v[8 * u + 2 * j + 1], slr, lr_wd);
+          w[j] = pack_bf16x2(lo, hi);
+        }
+        q.x = w[0];
+        q.y = w[1];
+        q.z = w[2];
+        q.w = w[3];
+        st_shared_v4(a, q);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const uint32_t a = pb + sw64_offset(k, lane >> 3) + 2 * (lane & 7);
+        const float w = param_new<T>(bf16_bits_to_float(ld_shared_u16(a)), v[k], slr, lr_wd);
+        st_shared_u16(a, float_to_bf16_bits(w));
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int x = md.transposed ? grow0 : gcol0, y = md.transposed ? gcol0 : grow0;
+    const uint64_t pol = l2_policy_evict_first();
+    tma_store_2d_hint(maps + TM_P, stage + LAST_P_OFF, x, y, pol);
+    if (SHADOW) tma_store_2d_hint(maps + TM_SH, stage + LAST_SHADOW_OFF, x, y, pol);
+    bulk_commit_group();
   }
 }
 
 template <int MODE>
 __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc& md, int grow0, int grow, bool row_ok,
                                              int gcol0, bool mirror, uint32_t (&acc)[32], const ChunkIn& in,
-                                             uint8_t* stage) {
+                                             uint8_t* stage, LastIo& io, int next_gcol0) {
   float (&v)[32] = reinterpret_cast<float (&)[32]>(acc);
   const int m = md.m;
   if (grow0 >= m) return;  // the warp's rows lie past the matrix: nothing to store (warp-uniform)
@@ -442,9 +555,22 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
     stage_and_store(stage, v, maps + (TM_X0_ST + ((args.iter & 1) ^ 1)), gcol0, grow0, false);
     return;
   }
-  if (!row_ok) return;
   // scaled_lr = lr * shape factor, formed in double and rounded once (triton_muon.py:424-431).
   const float slr = static_cast<float>(args.lr * md.lr_scale);
+  if (io.on) {  // warp-uniform: every lane takes part in the staged update
+    if (md.dtype == MAD_DTYPE_BF16)
+      write_params_tma<__nv_bfloat16, false>(md, maps, v, grow0, gcol0, slr, args.lr_wd, stage, io, args.status,
+                                             args.wait_limit);
+    else if (md.dtype == MAD_DTYPE_F32_MASTER)
+      write_params_tma<float, true>(md, maps, v, grow0, gcol0, slr, args.lr_wd, stage, io, args.status,
+                                    args.wait_limit);
+    else
+      write_params_tma<float, false>(md, maps, v, grow0, gcol0, slr, args.lr_wd, stage, io, args.status,
+                                     args.wait_limit);
+    if (!io.failed && next_gcol0 >= 0) last_p_issue(md, maps, stage, io, grow0, next_gcol0);
+    return;
+  }
+  if (!row_ok) return;
   if (md.dtype == MAD_DTYPE_BF16)
     write_params<__nv_bfloat16, false>(md, v, grow, gcol0, m, slr, args.lr_wd);
   else if (md.dtype == MAD_DTYPE_F32_MASTER)
@@ -461,28 +587,20 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
 // memory; polynomial: registers).
 template <int MODE>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull, uint64_t* tempty,
-                                              uint32_t tmem_base, uint8_t* stage, uint64_t* in_bar, uint32_t rank,
-                                              volatile int* abort_flag) {
+                                              uint32_t tmem_base, uint8_t* stage, uint64_t* in_bar, uint64_t* p_bar,
+                                              uint32_t rank, volatile int* abort_flag) {
   constexpr bool TMA_IN = is_update<MODE>();
   uint32_t in_phase = 0;
+  LastIo io;
+  io.bar = p_bar;
+  io.phase = 0;
+  io.on = 0;
+  io.failed = 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const int half = (warp - 2) >> 2;
   const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
   const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-  // This warp's rows and columns of tile t: rows of its CTA's 128-row block, its quarter; its half of the columns.
-  auto warp_rows0 = [&](const TileRef& r) { return r.tm * PAIR_M + static_cast<int>(rank) * BM + quad * 32; };
-  auto warp_col0 = [&](const TileRef& r) { return r.tn * BN + half * 128; };
-  // UPDATE_LAST: this CTA's first two tiles now, then at the end of tile t the
-  // tile after next -- about a tile's mainloop of lead time.
-  auto prefetch_tile = [&](int tt) {
-    if (MODE == UPDATE_LAST && tt < args.n_tiles) {
-      const TileRef r = args.tiles[tt];
-      prefetch_param_block(args.mats[r.mat], warp_rows0(r), warp_col0(r));
-    }
-  };
-  prefetch_tile(cid);
-  prefetch_tile(cid + ncl);
   int lt = 0;
   for (int t = cid; t < args.n_tiles; t += ncl, ++lt) {
     const TileRef tr = args.tiles[t];
@@ -509,6 +627,15 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
       tma_acquire_desc(args.tmaps + md.tmap_base + st);
     }
     if (lane == 0 && TMA_IN) tma_acquire_desc(in_map);
+    io.on = (MODE == UPDATE_LAST && md.p_tma && warp_rows && nch > 0) ? 1u : 0u;
+    if (io.on) {
+      const CUtensorMap* maps = args.tmaps + md.tmap_base;
+      if (lane == 0) {
+        tma_acquire_desc(maps + TM_P);
+        if (md.dtype == MAD_DTYPE_F32_MASTER) tma_acquire_desc(maps + TM_SH);
+      }
+      last_p_issue(md, maps, stage, io, grow0, col0);  // chunk 0's block arrives while the accumulator completes
+    }
     ChunkIn in[2];
     if (TMA_IN) {
       if (nch > 0 && warp_rows) in_issue(stage, in_bar, in_map, col0, grow0);
@@ -539,15 +666,16 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
         tmem_ld32_issue(tbase + 32 * (c + 1), acc[(c + 1) & 1]);
       }
       if (c < nch)
-        chunk_finish<MODE>(args, md, grow0, grow, row_ok, col0 + 32 * c, mirror, acc[c & 1], in[c & 1], stage);
+        chunk_finish<MODE>(args, md, grow0, grow, row_ok, col0 + 32 * c, mirror, acc[c & 1], in[c & 1], stage, io,
+                           c + 1 < nch ? col0 + 32 * (c + 1) : -1);
       if (c + 1 < nch) tmem_ld_wait(acc[(c + 1) & 1]);
     }
+    if (MODE == UPDATE_LAST && io.failed) *abort_flag = 1;
     // Accumulator drained: one arrival per warp on the leader's barrier.
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive_cluster(tempty_leader[acc_buf]);
     if (*abort_flag) break;
-    prefetch_tile(t + 2 * ncl);
   }
   if (lane == 0) bulk_wait_all();  // every output store has landed before the CTA retires
 }
@@ -559,20 +687,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   // Same layout in both CTAs of the pair: the pair MMA and the leader-side
   // barriers are addressed by identical shared-memory offsets.
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stage_out = ring + STAGES * STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + EPI_WARPS * STAGE_OUT_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* stage_out = ring + Smem<MODE>::STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + EPI_WARPS * Smem<MODE>::STAGE_OUT);
+  uint64_t* empty = full + MAX_STAGES;
+  uint64_t* tfull = empty + MAX_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* epi_in = drain + 1;  // one per epilogue warp: TMA fills of its input block
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_in + EPI_WARPS);
+  uint64_t* epi_in = drain + 1;          // one per epilogue warp: TMA fills of its X block
+  uint64_t* epi_p = epi_in + EPI_WARPS;  // one per epilogue warp: TMA fills of its parameter block (UPDATE_LAST)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_p + EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < Smem<MODE>::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -581,7 +710,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tempty[a], 2 * EPI_WARPS);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
-    for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&epi_in[w], 1);
+    for (int w = 0; w < EPI_WARPS; ++w) {
+      mbar_init(&epi_in[w], 1);
+      mbar_init(&epi_p[w], 1);
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -599,7 +731,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, abort_flag);
   } else {
-    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * STAGE_OUT_BYTES, &epi_in[warp - 2],
+    epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * Smem<MODE>::STAGE_OUT,
+                        &epi_in[warp - 2], &epi_p[warp - 2],
                         rank, abort_flag);
   }
   __syncthreads();
@@ -621,6 +754,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 template <int MODE>
 static int launch(const GemmArgs& args, cudaStream_t stream, const char* name) {
   if (args.n_tiles <= 0) return MAD_OK;
+  constexpr int SMEM_BYTES = Smem<MODE>::BYTES;
   if (cudaFuncSetAttribute(ns_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return fail_cuda("cudaFuncSetAttribute(ns_gemm_kernel)");

@@ -29,9 +29,9 @@ struct AdamEntry {
 };
 static_assert(sizeof(AdamEntry) == 64, "AdamEntry layout");
 
-constexpr int ADAM_THREADS = 256;
-constexpr int ADAM_VECS = 2;                           // 4-element vectors per thread and stream in a tile
-constexpr int ADAM_TILE = ADAM_THREADS * 4 * ADAM_VECS;  // elements per tile: 2048
+constexpr int ADAM_THREADS = 128;
+constexpr int ADAM_VECS = 1;                           // 4-element vectors per thread and stream in a tile
+constexpr int ADAM_TILE = ADAM_THREADS * 4 * ADAM_VECS;  // elements per tile: 512
 
 // ---------------------------------------------------------------- Muon
 constexpr int TM_XK0 = 0;   // X ping buffer, K-major box {64, 128}
@@ -45,7 +45,12 @@ constexpr int TM_GRAM_ST = 6;
 constexpr int TM_POLY_ST = 7;
 constexpr int TM_X0_ST = 8;
 constexpr int TM_X1_ST = 9;
-constexpr int TMAPS_PER_MAT = 10;
+// Parameter write of the last update: 32x32 boxes of the parameter (its own
+// type and orientation; 128-byte swizzle for float32, 64-byte for bf16) and
+// of the bf16 shadow of a float32 master.  Valid when MatDesc::p_tma is set.
+constexpr int TM_P = 10;
+constexpr int TM_SH = 11;
+constexpr int TMAPS_PER_MAT = 12;
 
 constexpr int PREP_TILE = 64;  // prep works on 64x64 tiles of the parameter
 constexpr int PREP_PARTIALS_PER_TILE = 8;  // one partial sum of squares per prep warp
@@ -70,7 +75,7 @@ struct MatDesc {
   int32_t tmap_base;     // index of this matrix's first tensor map
   int32_t vec;           // 4-element vectors legal for p, g, mom (and shadow) on every row
   int32_t dtype;         // MAD_DTYPE_*: 0 float32, 1 bf16, 2 float32 master + bf16 grad/shadow
-  int32_t pad;
+  int32_t p_tma;         // 1: TM_P (and TM_SH for dtype 2) describe the parameter; else per-thread writes
   void* shadow;          // dtype 2: bf16 copy of the updated parameter, same layout as p
 };
 static_assert(sizeof(MatDesc) == 136, "MatDesc layout");

@@ -16,6 +16,7 @@ that is rebuilt only when a tensor's storage changes.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from collections.abc import Iterable
 
 import torch
@@ -156,28 +157,50 @@ class TritonAdamW:
             self.v[param] = torch.zeros_like(param, dtype=torch.float32)
         self.masters = None  # {param: float32 master} in mixed-precision mode (MuonAdamW(master_weights=True))
         self._table = AdamWTable()
+        self._signature = None   # (gradients, by weak reference; parameter and gradient addresses) last planned
 
     def _active(self):
         quads = []
+        masters = self.masters
         for p in self.model_params:
-            if p.grad is None:
+            g = p.grad
+            if g is None:
                 continue
-            _check_tensor(p, "AdamW parameter")
-            _check_tensor(p.grad, "AdamW gradient", p.dtype)
-            if self.masters is not None:
-                quads.append((self.masters[p], p.grad, self.m[p], self.v[p], p.data))
+            if not (p.is_cuda and g.is_cuda and p.dtype in DTYPE_CODES and g.dtype == p.dtype
+                    and p.is_contiguous() and g.is_contiguous()):
+                _check_tensor(p, "AdamW parameter")          # raises the specific error
+                _check_tensor(g, "AdamW gradient", p.dtype)
+            if masters is not None:
+                quads.append((masters[p], g, self.m[p], self.v[p], p.detach()))
             else:
-                quads.append((p.data, p.grad, self.m[p], self.v[p]))
+                quads.append((p.detach(), g, self.m[p], self.v[p]))
         return quads
 
     @torch.no_grad()
     def step(self):
-        """One AdamW update of every parameter that has a gradient (triton_adam.py:132-153)."""
+        """One AdamW update of every parameter that has a gradient (triton_adam.py:132-153).
+
+        The host side is one pass over the parameters: when every parameter
+        and gradient is the tensor (and storage) of the previous step, the
+        planned table is launched as is; otherwise the tensors are validated
+        and the table re-planned or patched.
+        """
         self.step_num += 1
-        quads = self._active()
-        if not quads:
+        grads = [p.grad for p in self.model_params]
+        addrs = tuple(g.data_ptr() if g is not None else 0 for g in grads) + \
+            tuple(p.data_ptr() for p in self.model_params)
+        sig = self._signature
+        if sig is None or addrs != sig[1] or any((r() if r is not None else None) is not g
+                                                 for r, g in zip(sig[0], grads)):
+            quads = self._active()
+            if not quads:
+                self._signature = None
+                return
+            self._table.ensure(quads, quads[0][0].device)
+            # Weak references: a gradient dropped by zero_grad(set_to_none=True) is freed, not kept alive here.
+            self._signature = ([weakref.ref(g) if g is not None else None for g in grads], addrs)
+        elif self._table.n_tiles == 0:
             return
-        self._table.ensure(quads, quads[0][0].device)
         if getattr(self, "_timer", None) is not None:
             self._timer.mark("adamw")
         self._table.launch(lr=self.lr, beta1=self.beta1, beta2=self.beta2, eps=self.eps,
