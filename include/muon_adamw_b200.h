@@ -276,6 +276,14 @@ int mad_peer_push(const void* src, int64_t bytes, const mad_peer_set* peers, voi
 int mad_muon_read_status(const mad_muon_plan_info* info, void* dev_table, uint32_t* status, int32_t clear,
                          void* stream);
 
+/* The Newton-Schulz GEMMs (persistent: one CTA per SM) leave `sms` SMs free
+ * from the next launch on, rounded up to whole CTA pairs (no counterpart in
+ * the single-GPU reference).  A sharded step's exchange kernels (NCCL's
+ * all-gather) launched beside the GEMMs on other streams then run at once
+ * instead of taking SMs the GEMM's next launch is waiting for.  0 (default):
+ * every SM. */
+int mad_set_gemm_sm_reserve(int32_t sms);
+
 /* Test hook (no counterpart in the reference): the next n_launches
  * Newton-Schulz Gram launches of this process run with an idle TMA producer
  * and a ~10 ms barrier-wait limit, so their waits expire with no copy or MMA

@@ -63,8 +63,10 @@ struct Smem {
   static constexpr int BYTES = STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT + 1024 + 1024;  // + barriers, alignment
 };
 static_assert(Smem<GRAM>::BYTES <= 227 * 1024 && Smem<UPDATE_LAST>::BYTES <= 227 * 1024, "shared memory per CTA");
-// Offsets inside an UPDATE_LAST warp's staging area.
-constexpr int LAST_SHADOW_OFF = 0, LAST_X_OFF = 2048, LAST_P_OFF = 4096;
+// Offsets inside a warp's staging area: the X block of the update kernels'
+// a*X term, and UPDATE_LAST's bf16 shadow and parameter blocks.
+constexpr int X_IN_OFF = 2048, LAST_SHADOW_OFF = 0, LAST_P_OFF = 4096;
+static_assert(X_IN_OFF + 2048 <= LAST_P_OFF && LAST_SHADOW_OFF + 2048 <= X_IN_OFF, "staging areas overlap");
 
 // UPDATE_LAST is the update of the final iteration, which writes the
 // parameters; it is a separate instantiation so the common path can keep two
@@ -240,7 +242,7 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 __device__ __forceinline__ void in_issue(uint8_t* stage, uint64_t* bar, const CUtensorMap* map, int x, int y) {
   if ((threadIdx.x & 31) == 0) {
     mbar_arrive_expect_tx(bar, 2048);
-    tma_load_2d(stage + 2048, map, bar, x, y);
+    tma_load_2d(stage + X_IN_OFF, map, bar, x, y);
   }
 }
 
@@ -251,7 +253,7 @@ __device__ __forceinline__ void in_take(uint8_t* stage, uint64_t* bar, uint32_t&
   if (!mbar_wait(bar, phase, status, DEV_ERR_MBAR_TIMEOUT_EPILOGUE)) *abort_flag = 1;
   phase ^= 1u;
   const int lane = threadIdx.x & 31;
-  const uint32_t base = smem_u32(stage + 2048);
+  const uint32_t base = smem_u32(stage + X_IN_OFF);
 #pragma unroll
   for (int j = 0; j < 4; ++j) q[j] = ld_shared_v4(base + static_cast<uint32_t>(lane * 64 + 16 * (j ^ ((lane >> 1) & 3))));
   // These generic-proxy reads must be ordered before the next TMA (async-proxy)
@@ -751,6 +753,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// SMs the persistent GEMM leaves free for kernels that must run beside it
+// (the NCCL all-gather of a sharded step): set by mad_set_gemm_sm_reserve.
+std::atomic<int> g_reserved_sms{0};
+
 template <int MODE>
 static int launch(const GemmArgs& args, cudaStream_t stream, const char* name) {
   if (args.n_tiles <= 0) return MAD_OK;
@@ -779,6 +785,9 @@ static int launch(const GemmArgs& args, cudaStream_t stream, const char* name) {
       return fail_cuda("cudaOccupancyMaxActiveClusters(ns_gemm_kernel)");
     if (dev < 16) max_pairs[dev] = pairs;
   }
+  // SMs left to other kernels (mad_set_gemm_sm_reserve): whole CTA pairs fewer.
+  const int reserve_pairs = (g_reserved_sms.load(std::memory_order_relaxed) + 1) / 2;
+  if (reserve_pairs > 0) pairs = pairs - reserve_pairs > 1 ? pairs - reserve_pairs : 1;
   const int grid_pairs = args.n_tiles < pairs ? args.n_tiles : pairs;
   ns_gemm_kernel<MODE><<<2 * grid_pairs, NUM_THREADS, SMEM_BYTES, stream>>>(args);
   return check_launch(name);
@@ -833,5 +842,15 @@ extern "C" int mad_debug_expire_next_waits(int32_t n_launches) {
   mad::clear_error();
   if (n_launches < 0) return mad::fail(MAD_ERR_INVALID, "mad_debug_expire_next_waits: negative count");
   mad::ns::g_expire_gram_launches.store(n_launches);
+  return MAD_OK;
+}
+
+// The Newton-Schulz GEMMs of this process run on (SMs - sms) SMs from the next
+// launch on, rounded to CTA pairs, so kernels launched beside them on other
+// streams find SMs free.  0 (the default) uses every SM.
+extern "C" int mad_set_gemm_sm_reserve(int32_t sms) {
+  mad::clear_error();
+  if (sms < 0 || sms > 1024) return mad::fail(MAD_ERR_INVALID, "mad_set_gemm_sm_reserve: %d SMs out of range", sms);
+  mad::ns::g_reserved_sms.store(sms);
   return MAD_OK;
 }

@@ -103,6 +103,7 @@ SIGNATURES = {
     "mad_copy_async": (ctypes.c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "mad_peer_push": (ctypes.c_int, [c_void_p, c_int64, ctypes.POINTER(PeerSet), c_void_p]),
     "mad_debug_expire_next_waits": (ctypes.c_int, [c_int32]),
+    "mad_set_gemm_sm_reserve": (ctypes.c_int, [c_int32]),
     "mad_adamw_set_grads": (ctypes.c_int, [c_void_p, c_int64, ctypes.POINTER(c_void_p), c_int32, c_void_p]),
     "mad_muon_set_grads": (ctypes.c_int, [ctypes.POINTER(MuonPlanInfo), c_void_p, ctypes.POINTER(c_void_p),
                                           c_void_p]),

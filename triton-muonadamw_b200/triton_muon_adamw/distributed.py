@@ -174,10 +174,13 @@ class CudaBackend:
 
     PUSH_MODES = ("auto", "nccl", "copy_engine", "kernel", "hybrid")
 
-    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5):
+    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms: int = 0):
         if push not in self.PUSH_MODES:
             raise ValueError(f"push must be one of {self.PUSH_MODES}, got {push!r}")
+        if not 0 <= int(reserve_sms) <= 64:
+            raise ValueError(f"reserve_sms must be in 0..64, got {reserve_sms!r}")
         self.push = push
+        self.reserve_sms = int(reserve_sms)
         self.ce_splits = max(1, int(ce_splits))
         self.ce_fraction = float(ce_fraction)
         self.adam_table = AdamWTable()
@@ -277,7 +280,7 @@ class CudaBackend:
         plan = self.plans.setdefault(bucket, MuonPlan())
         plan.ensure(triples, adjust_lr_fn, triples[0][0].device)
         run_muon_plan(plan, beta=beta, nesterov=nesterov, a=a, b=b, c=c, ns_steps=ns_steps, eps=eps, lr=lr,
-                      weight_decay=weight_decay, timer=timer, reduce=reduce)
+                      weight_decay=weight_decay, timer=timer, reduce=reduce, reserve_sms=self.reserve_sms)
 
     def status(self) -> int:
         st = 0

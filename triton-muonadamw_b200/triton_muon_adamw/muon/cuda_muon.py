@@ -120,17 +120,19 @@ class MuonPlan:
 
 
 def run_muon_plan(plan: MuonPlan, *, beta, nesterov, a, b, c, ns_steps, eps, lr, weight_decay, timer=None,
-                  stream=None, reduce=None) -> None:
+                  stream=None, reduce=None, reserve_sms: int = 0) -> None:
     """Launch the whole Muon branch for a plan on the current (or given) stream.
 
     Without a timer this is one C call (``mad_muon_step_multi``); with one,
     the same launches are issued phase by phase with a CUDA event between
     them so each kernel can be timed on its launching stream.  ``reduce`` (a
-    ``GradReduce``) makes the prep sum each gradient over ranks.
+    ``GradReduce``) makes the prep sum each gradient over ranks;
+    ``reserve_sms`` SMs are left free by the GEMMs (``mad_set_gemm_sm_reserve``).
     """
     if plan.n_mats == 0:
         return
     lib = _lib.load()
+    _lib.check(lib.mad_set_gemm_sm_reserve(int(reserve_sms)), "mad_set_gemm_sm_reserve")
     info, tab, st = ctypes.byref(plan.info), plan.table.data_ptr(), _lib.stream_handle(stream)
     nest = 1 if nesterov else 0
     if timer is None:

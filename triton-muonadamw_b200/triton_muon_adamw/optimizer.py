@@ -171,6 +171,11 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         bf16 gradients would give, bit for bit.  Sharded, each rank keeps the
         masters of what it owns and the all-gather moves bf16 (half the bytes).
         Checkpoints carry the masters (``"master_param"`` per parameter).
+    reserve_sms:
+        With more than one rank, SMs the Newton-Schulz GEMMs leave free (0..64,
+        rounded up to pairs) so that the parameter exchange's kernels (NCCL's
+        all-gather) run beside them instead of waiting for -- and delaying --
+        a GEMM launch.  0 (default): the GEMMs use every SM.
     """
 
     def __init__(
@@ -183,6 +188,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         reduce_grads: Literal["mean", "sum"] | None = None,
         peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid"] = "auto",
         master_weights: bool = False,
+        reserve_sms: int = 0,
     ) -> None:
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
@@ -198,7 +204,8 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         if process_group is not None and torch.distributed.get_world_size(process_group) > 1:
             from .distributed import ShardedMuonAdamW  # noqa: PLC0415
             self.distributed = ShardedMuonAdamW(adam_params, muon_params, muon_config, adam_config, process_group,
-                                                reduce_grads=reduce_grads, backend=CudaBackend(push=peer_push),
+                                                reduce_grads=reduce_grads,
+                                                backend=CudaBackend(push=peer_push, reserve_sms=reserve_sms),
                                                 master_weights=self.master_weights)
             self.adamw = self.distributed.adamw
             self.muon = self.distributed.muon
