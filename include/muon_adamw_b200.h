@@ -4,9 +4,10 @@
  * Plain pointers and sizes only.  All pointers named param/grad/exp_avg/
  * exp_avg_sq/momentum/dev_* are CUDA device pointers; `stream` is a
  * cudaStream_t passed as void*.  Every function returns 0 (MAD_OK) on success
- * or a MAD_ERR_* code, with a message from mad_last_error().  No function
- * allocates device memory: callers size buffers with the *_bytes / *_plan_size
- * functions and pass them in.
+ * or a MAD_ERR_* code, with a message from mad_last_error().  Apart from
+ * mad_ipc_alloc (device buffers other processes of the node map, for the
+ * multi-GPU paths), no function allocates device memory: callers size
+ * buffers with the *_bytes / *_plan_size functions and pass them in.
  *
  * Each entry point replaces one piece of the reference's Python/Triton path
  * (reference paths relative to its "MuonAdamW package/" directory):
@@ -23,6 +24,9 @@
  *   mad_ns_update          triton_muon_adamw/muon/triton_muon.py:281-310 solve_ns_kernel_3, and on the
  *                          last iteration the muon_step epilogue :365-372
  *   mad_muon_step_multi    triton_muon_adamw/muon/triton_muon.py:414-448 TritonMuon.step
+ *   mad_adamw_set_grads,
+ *   mad_muon_set_grads     the reference reads p.grad afresh on every step (triton_adam.py:137-153,
+ *                          triton_muon.py:414-448); these follow new gradient tensors without re-planning
  */
 #ifndef MUON_ADAMW_B200_H
 #define MUON_ADAMW_B200_H
