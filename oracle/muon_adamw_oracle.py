@@ -66,7 +66,8 @@ def adamw_update_(p, g, m, v, *, lr, beta1, beta2, eps, weight_decay, bias1, bia
     moments, then decoupled decay applied multiplicatively to the old value.
     The kernel there receives its scalars as float32 and forms ``1-beta1``,
     ``1-beta2`` and ``1-lr*wd`` in float32; every operation below is one
-    float32 rounding, in the kernel's order.
+    IEEE float32 rounding (division and square root correctly rounded), in
+    the kernel's order.
 
     A bf16 parameter (and gradient) is read as float32, the arithmetic is the
     same, and the new value is rounded to bf16 on the store; the moments stay
@@ -79,10 +80,18 @@ def adamw_update_(p, g, m, v, *, lr, beta1, beta2, eps, weight_decay, bias1, bia
     g = g.to(f)
     m_t = (b1 * m) + ((one - b1) * g)
     v_t = (b2 * v) + ((one - b2) * (g * g))
-    m_c = m_t / torch.tensor(bias1, dtype=f)
-    v_c = v_t / torch.tensor(bias2, dtype=f)
+    # IEEE float32 division and square root, as the formula is written (and as
+    # the Triton interpreter, whose goldens pin this restatement, evaluates it):
+    # torch's CPU `tensor / 0-dim tensor` multiplies by the reciprocal instead,
+    # and its vectorised float32 sqrt is not correctly rounded -- each one ulp
+    # off on a fraction of a percent of elements.  A float64 result rounded once
+    # to float32 is the correctly rounded float32 result (double rounding is
+    # innocuous for division and square root when 53 >= 2*24 + 2).
+    m_c = (m_t.double() / float(torch.tensor(bias1, dtype=f))).to(f)
+    v_c = (v_t.double() / float(torch.tensor(bias2, dtype=f))).to(f)
+    denom = torch.sqrt(v_c.double()).to(f) + torch.tensor(eps, dtype=f)
     decayed = (one - lr_f * wd_f) * p.to(f)
-    p.copy_(decayed - lr_f * (m_c / (torch.sqrt(v_c) + torch.tensor(eps, dtype=f))))
+    p.copy_(decayed - lr_f * (m_c / denom))
     m.copy_(m_t)
     v.copy_(v_t)
 

@@ -63,6 +63,39 @@ def test_adamw_single_tensor_vs_oracle(cuda_device, numel, offset):
     torch.testing.assert_close(v.cpu(), vc, atol=1e-12, rtol=2e-6)
 
 
+@pytest.mark.parametrize("beta1,beta2,step", [(0.9, 0.999, 1), (0.9, 0.95, 7), (0.9, 0.999, 1000), (0.0, 0.5, 3)])
+def test_adamw_is_bit_exact_vs_oracle_across_magnitudes(cuda_device, beta1, beta2, step):
+    """Every rounding of the AdamW kernel against the float32 oracle, bit for bit: operands spanning
+    ~70 orders of magnitude, both signs, zeros, bias corrections of early and late steps -- including the
+    division by the bias corrections, which the kernel forms from a correctly rounded reciprocal and one
+    FMA correction (exact for its operand window; other operands take the IEEE division)."""
+    L = _lib()
+    lib = L.load()
+    gen = torch.Generator().manual_seed(step)
+    n = 1 << 21
+
+    def log_uniform(lo, hi, signed=True):
+        mag = torch.pow(10.0, torch.rand(n, generator=gen, dtype=torch.float64) * (hi - lo) + lo)
+        if signed:
+            mag = mag * (torch.randint(0, 2, (n,), generator=gen) * 2 - 1)
+        return mag.float()
+
+    p, g, m, v = log_uniform(-30, 3), log_uniform(-30, 3), log_uniform(-35, 2), log_uniform(-38, 3, signed=False)
+    g[::97] = 0.0
+    m[::89] = 0.0
+    v[::83] = 0.0
+    dev = [t.to(cuda_device) for t in (p, g, m, v)]
+    b1, b2 = adamw_bias_corrections(beta1, beta2, step)
+    L.check(lib.mad_adamw_step(dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), dev[3].data_ptr(), n, 3e-4,
+                               b1, b2, beta1, beta2, 0.01, 1e-8, L.stream_handle()))
+    adamw_update_(p, g, m, v, lr=3e-4, beta1=beta1, beta2=beta2, eps=1e-8, weight_decay=0.01, bias1=b1, bias2=b2)
+    torch.cuda.synchronize()
+    for got, want, name in zip((dev[0], dev[2], dev[3]), (p, m, v), ("param", "exp_avg", "exp_avg_sq")):
+        got = got.cpu()
+        same = (got == want) | (torch.isnan(got) & torch.isnan(want))
+        assert bool(same.all()), f"{name}: {int((~same).sum())} of {n} differ, e.g. {got[~same][:4]} vs {want[~same][:4]}"
+
+
 def test_adamw_branch_vs_reference_triton_golden(cuda_device):
     """Reference TritonAdamW (Triton interpreter) golden, incl. a None gradient."""
     from triton_muon_adamw.adamw import TritonAdamW

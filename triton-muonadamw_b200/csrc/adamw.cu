@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -31,14 +32,35 @@ namespace mad {
 
 struct AdamScalars {
   float lr, beta1, beta2, one_m_beta1, one_m_beta2, eps, decay, bias1, bias2;
+  float rbias1, rbias2;  // RN(1/bias1), RN(1/bias2): correctly rounded reciprocals, formed on the host
   GradReduce red;  // red.n > 0: the gradient is the mean of every rank's copy (peer memory)
 };
+
+// a / b for a divisor b fixed for the whole launch, with rb = RN(1/b):
+// Markstein's correction step (Markstein 1990; Muller et al., Handbook of
+// Floating-Point Arithmetic, on FMA-based division) -- q = RN(a rb), the exact
+// residual r = a - q b by FMA, RN(q + r rb) -- is the correctly rounded
+// quotient whenever neither it nor the residual leaves the normal range, which
+// the operand window below guarantees for divisors 1 >= b >= 2^-40 (rb == 0
+// marks a divisor outside that range).  Other operands (zero, subnormal, huge,
+// inf, NaN) take the IEEE division.  Three instructions instead of a full
+// division on the AdamW path, which at the power-capped SM clock of the
+// optimizer step is close to issue-bound.
+__device__ __forceinline__ float div_uniform(float a, float b, float rb) {
+  const float aa = fabsf(a);
+  if (__builtin_expect(rb != 0.f && aa >= 0x1p-80f && aa <= 0x1p80f, 1)) {
+    const float q = __fmul_rn(a, rb);
+    const float r = __fmaf_rn(-q, b, a);
+    return __fmaf_rn(r, rb, q);
+  }
+  return __fdiv_rn(a, b);
+}
 
 __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v, const AdamScalars& s) {
   const float mt = __fadd_rn(__fmul_rn(s.beta1, m), __fmul_rn(s.one_m_beta1, g));
   const float vt = __fadd_rn(__fmul_rn(s.beta2, v), __fmul_rn(s.one_m_beta2, __fmul_rn(g, g)));
-  const float mc = __fdiv_rn(mt, s.bias1);
-  const float vc = __fdiv_rn(vt, s.bias2);
+  const float mc = div_uniform(mt, s.bias1, s.rbias1);
+  const float vc = div_uniform(vt, s.bias2, s.rbias2);
   const float step = __fdiv_rn(mc, __fadd_rn(__fsqrt_rn(vc), s.eps));
   p = __fsub_rn(__fmul_rn(s.decay, p), __fmul_rn(s.lr, step));
   m = mt;
@@ -209,6 +231,25 @@ __global__ void __launch_bounds__(ADAM_THREADS, 12) adamw_single_kernel(AdamEntr
   }
 }
 
+// RN(1/b) for a divisor 1 >= b >= 2^-40 (else 0: div_uniform then divides):
+// the float nearest 1/b, chosen among the double quotient's float rounding and
+// its two neighbours by the exact residual |1 - b y| (b y is exact in double:
+// 24 x 24 significant bits).
+static float reciprocal_rn(float b) {
+  if (!(b >= 0x1p-40f && b <= 1.0f)) return 0.0f;
+  const float y0 = static_cast<float>(1.0 / static_cast<double>(b));
+  float best = y0;
+  double best_err = std::fabs(1.0 - static_cast<double>(b) * static_cast<double>(y0));
+  for (float y : {std::nextafter(y0, 0.f), std::nextafter(y0, INFINITY)}) {
+    const double err = std::fabs(1.0 - static_cast<double>(b) * static_cast<double>(y));
+    if (err < best_err) {
+      best = y;
+      best_err = err;
+    }
+  }
+  return best;
+}
+
 // The reference kernel receives its scalars as float32 and forms 1-beta1,
 // 1-beta2 and 1-lr*wd in float32 (triton_adam.py:53-58); so do we.
 static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, float wd, float bias1, float bias2) {
@@ -224,6 +265,8 @@ static AdamScalars make_scalars(float lr, float beta1, float beta2, float eps, f
   s.decay = 1.0f - lr_wd;
   s.bias1 = bias1;
   s.bias2 = bias2;
+  s.rbias1 = reciprocal_rn(bias1);
+  s.rbias2 = reciprocal_rn(bias2);
   return s;
 }
 
