@@ -264,6 +264,12 @@ def main():
     ap.add_argument("--realloc-grads", action="store_true",
                     help="alternate every step between two sets of gradient tensors (new .grad addresses each "
                          "step, as zero_grad(set_to_none=True) + backward gives): the plans patch the addresses")
+    ap.add_argument("--cases", default=None,
+                    help="sweeps only: comma-separated case names to run (adamw_sweep: 1M,16M,64M,256M,ragged_10k; "
+                         "ns_isolated: SHAPExBATCH, e.g. 4096x14336x32)")
+    ap.add_argument("--impls", default=None,
+                    help="adamw_sweep only: comma-separated implementations (ours,reference_triton,torch_fused); "
+                         "profiler captures leave out the reference's ragged case (10,000 launches a step)")
     ap.add_argument("--no-verify", action="store_true",
                     help="at N>1, skip the post-timing check of every replica against a single-GPU recomputation")
     args = ap.parse_args()
@@ -875,6 +881,8 @@ def run_adamw_sweep(args):
     cases = [("1M", [1 << 20]), ("16M", [1 << 24]), ("64M", [1 << 26]), ("256M", [1 << 28])]
     rg = torch.Generator().manual_seed(7)
     cases.append(("ragged_10k", torch.randint(1, 65537, (10000,), generator=rg).tolist()))
+    if args.cases:
+        cases = [c for c in cases if c[0] in args.cases.split(",")]
     out = []
     for name, sizes in cases:
         numel = sum(sizes)
@@ -883,6 +891,8 @@ def run_adamw_sweep(args):
         if ref_mod is not None:
             impls.append(("reference_triton", lambda ps: ref_mod.adamw.triton_adam.TritonAdamW(ps, **hp)))
         impls.append(("torch_fused", lambda ps: torch.optim.AdamW(ps, fused=True, **hp)))
+        if args.impls:
+            impls = [i for i in impls if i[0] in args.impls.split(",")]
         for impl, make in impls:
             # The reference launches grid (rows, cdiv(cols, 512)) per tensor (triton_adam.py:92-94), and a 1-D
             # tensor is one row: beyond 65535 * 512 elements grid.y exceeds the CUDA limit and the launch fails.
@@ -902,13 +912,14 @@ def run_adamw_sweep(args):
             row[impl] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3)}
             del opt, params
             torch.cuda.empty_cache()
-        if "reference_triton" in row:
+        if "reference_triton" in row and "ours" in row:
             row["speedup_vs_reference_triton"] = round(row["reference_triton"]["ms"] / row["ours"]["ms"], 2)
-        row["speedup_vs_torch_fused"] = round(row["torch_fused"]["ms"] / row["ours"]["ms"], 2)
+        if "torch_fused" in row and "ours" in row:
+            row["speedup_vs_torch_fused"] = round(row["torch_fused"]["ms"] / row["ours"]["ms"], 2)
         out.append(row)
         print(json.dumps(row), file=sys.stderr, flush=True)
-    big = next(r for r in out if r["case"] == "256M")
-    print(json.dumps({"metric": "AdamW HBM GB/s (C2 sweep; value: 256M-element case)", "value": big["ours"]["gbs"],
+    big = next((r for r in out if r["case"] == "256M" and "ours" in r), None) or next(r for r in out if "ours" in r)
+    print(json.dumps({"metric": f"AdamW HBM GB/s (C2 sweep; value: {big['case']} case)", "value": big["ours"]["gbs"],
                       "unit": "GB/s", "higher_is_better": True, "n_gpus": 1, "steps": max(3, args.steps),
                       "dtype": "fp32", "data": "synthetic (seeded; params N(0,0.02), grads N(0,1e-2))",
                       "peak": hbm, "peak_kind": f"{peak_src} HBM copy", "config": {"workload": "C2 AdamW sweep"},
@@ -929,8 +940,11 @@ def run_ns_sweep(args):
     _, tf_burst, tf_sus, peak_src = measured_peaks()
     gen = torch.Generator(device=dev).manual_seed(0)
     out = []
+    wanted = set(args.cases.split(",")) if args.cases else None
     for shape in [(1024, 1024), (4096, 4096), (4096, 14336), (14336, 4096)]:
         for batch in (1, 8, 32):
+            if wanted is not None and f"{shape[0]}x{shape[1]}x{batch}" not in wanted:
+                continue
             for ns in (5, 6):
                 params = []
                 for _ in range(batch):
@@ -968,8 +982,9 @@ def run_ns_sweep(args):
                 del opt, params
                 torch.cuda.empty_cache()
     best = max(out, key=lambda r: r["tflops"])
-    head = next(r for r in out if r["shape"] == [4096, 14336] and r["batch"] == 32 and r["ns_steps"] == 5)
-    print(json.dumps({"metric": "Newton-Schulz TFLOP/s (C3; value: 32 x 4096x14336, ns 5)", "value": head["tflops"],
+    head = next((r for r in out if r["shape"] == [4096, 14336] and r["batch"] == 32 and r["ns_steps"] == 5), best)
+    print(json.dumps({"metric": f"Newton-Schulz TFLOP/s (C3; value: {head['batch']} x {head['shape'][0]}x"
+                                f"{head['shape'][1]}, ns {head['ns_steps']})", "value": head["tflops"],
                       "unit": "TFLOP/s", "higher_is_better": True, "n_gpus": 1, "dtype": "bf16 (fp32 accumulate)",
                       "data": "synthetic (bf16-valued N(0,1) matrices, seeded)", "peak_sustained": tf_sus,
                       "peak_burst": tf_burst, "peak_kind": f"{peak_src} bf16", "best_case": best,
