@@ -27,9 +27,18 @@
 // (one accumulator row and half the columns per thread).  Operands: X Xᵀ and
 // A A read two K-major tiles; B X reads B K-major and X MN-major (its rows are
 // the K index).
+//
+// Tiles are handed out dynamically: the leader's producer thread takes the
+// next tile index from a counter in the plan header (one atomic per tile) and
+// publishes it to both CTAs of its pair through a small ring in shared
+// memory, so a pair that starts late -- its SMs held by a kernel running
+// beside the GEMM, such as a collective -- takes fewer tiles instead of
+// finishing its share after everyone else.  Tile results do not depend on
+// which pair computes them.
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
 
 #include "capi_common.h"
 #include "elem_io.cuh"
@@ -85,11 +94,71 @@ struct GemmArgs {
   float lr_wd;
   double lr;
   unsigned int* status;
+  int32_t* sched;        // {next tile, retired pairs}: zero at launch, reset by the last pair
   long long wait_limit;  // SM cycles before a barrier wait gives up
   int idle_producer;     // test launches only: the producer issues no loads, so the waits expire
 };
 
 __device__ __forceinline__ int k_extent(int mode, const MatDesc& md) { return mode == GRAM ? md.n : md.m; }
+
+// ---------------------------------------------------------------- tile scheduler
+// Ring of tile indices, one copy in each CTA of the pair.  Entry j is written
+// by the leader's producer (a tile index, or -1 when none is left) and read by
+// every other role of the pair: the leader's MMA thread and epilogue warps,
+// the peer's producer and epilogue warps.  Each reader arrives on the leader's
+// `empty` barrier of the entry; the producer reuses it after all of them.
+constexpr int SCHED_DEPTH = 8;
+constexpr uint32_t SCHED_READERS = 1 + EPI_WARPS + 1 + EPI_WARPS;
+
+struct Sched {
+  int32_t* slot;     // [SCHED_DEPTH]
+  uint64_t* full;    // [SCHED_DEPTH], one arrival (the leader's producer)
+  uint64_t* empty;   // [SCHED_DEPTH], SCHED_READERS arrivals; only the leader's are used
+};
+
+// Leader producer: takes the next tile and publishes it as entry j.  False if
+// the entry's previous readers did not release it in time.
+__device__ __forceinline__ bool sched_publish(const GemmArgs& args, const Sched& sc, int j, int* tile) {
+  const int s = j % SCHED_DEPTH;
+  const uint32_t ph = static_cast<uint32_t>((j / SCHED_DEPTH) & 1);
+  if (!mbar_wait_cluster(&sc.empty[s], ph ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_PRODUCER, args.wait_limit))
+    return false;
+  int t = atomicAdd(&args.sched[0], 1);
+  if (t >= args.n_tiles) t = -1;
+  sc.slot[s] = t;
+  st_shared_cluster_u32(mapa_shared(smem_u32(&sc.slot[s]), 1), t);
+  mbar_arrive(&sc.full[s]);
+  mbar_arrive_cluster(mapa_shared(smem_u32(&sc.full[s]), 1));
+  *tile = t;
+  return true;
+}
+
+// Any other role: waits for entry j and reads it (every lane of a warp may
+// call this; `release` then runs on one lane after the warp has read it).
+__device__ __forceinline__ bool sched_take(const GemmArgs& args, const Sched& sc, int j, unsigned int err_bit,
+                                           int* tile) {
+  const int s = j % SCHED_DEPTH;
+  const uint32_t ph = static_cast<uint32_t>((j / SCHED_DEPTH) & 1);
+  if (!mbar_wait_cluster(&sc.full[s], ph, args.status, err_bit, args.wait_limit)) return false;
+  *tile = *reinterpret_cast<volatile int32_t*>(&sc.slot[s]);
+  return true;
+}
+
+__device__ __forceinline__ void sched_release(const Sched& sc, int j) {
+  mbar_arrive_cluster(mapa_shared(smem_u32(&sc.empty[j % SCHED_DEPTH]), 0));
+}
+
+// Leader producer, once per launch on every path: the last pair to finish
+// taking tiles resets the counter for the next launch on the stream.
+__device__ __forceinline__ void sched_retire(const GemmArgs& args) {
+  __threadfence();
+  const int done = atomicAdd(&args.sched[1], 1);
+  if (done == static_cast<int>(gridDim.x >> 1) - 1) {
+    __threadfence();
+    atomicExch(&args.sched[0], 0);
+    atomicExch(&args.sched[1], 0);
+  }
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(lo))) |
@@ -98,13 +167,36 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 template <int MODE>
 __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                              uint32_t rank, volatile int* abort_flag) {
+                                              const Sched& sc, uint32_t rank, volatile int* abort_flag) {
   int stage = 0;
   uint32_t phase = 0;
   const int cur = args.iter & 1;
-  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-  bool ok = !args.idle_producer;
-  for (int t = cid; t < args.n_tiles && ok; t += ncl) {
+  if (args.idle_producer) {
+    // Test launches: one tile is handed out and nothing is loaded, so the
+    // MMA and epilogue waits of that tile expire.
+    int t;
+    if (rank == 0) {
+      sched_publish(args, sc, 0, &t);
+      sched_retire(args);
+    }
+    return;
+  }
+  bool ok = true;
+  for (int j = 0; ok; ++j) {
+    int t;
+    if (rank == 0) {
+      if (!sched_publish(args, sc, j, &t)) {
+        *abort_flag = 1;
+        break;
+      }
+    } else {
+      if (!sched_take(args, sc, j, DEV_ERR_MBAR_TIMEOUT_PRODUCER, &t)) {
+        *abort_flag = 1;
+        break;
+      }
+      sched_release(sc, j);
+    }
+    if (t < 0) break;
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
     const CUtensorMap* maps = args.tmaps + md.tmap_base;
@@ -148,6 +240,7 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
       }
     }
   }
+  if (rank == 0) sched_retire(args);
 }
 
 // Leader CTA only: one thread issues the pair MMAs and returns each smem stage
@@ -155,13 +248,19 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
 template <int MODE>
 __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                          uint64_t* tfull, uint64_t* tempty, uint64_t* drain, uint32_t tmem_base,
-                                         volatile int* abort_flag) {
+                                         const Sched& sc, volatile int* abort_flag) {
   constexpr uint32_t IDESC = idesc_bf16_f32(PAIR_M, BN, false, is_update<MODE>());
-  int stage = 0, lt = 0;
+  int stage = 0;
   uint32_t phase = 0;
   bool ok = true;
-  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-  for (int t = cid; t < args.n_tiles && ok; t += ncl, ++lt) {
+  for (int lt = 0; ok; ++lt) {
+    int t;
+    if (!sched_take(args, sc, lt, DEV_ERR_MBAR_TIMEOUT_MMA, &t)) {
+      *abort_flag = 1;
+      break;
+    }
+    sched_release(sc, lt);
+    if (t < 0) break;
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
     const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
@@ -590,7 +689,7 @@ __device__ __forceinline__ void chunk_finish(const GemmArgs& args, const MatDesc
 template <int MODE>
 __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tfull, uint64_t* tempty,
                                               uint32_t tmem_base, uint8_t* stage, uint64_t* in_bar, uint64_t* p_bar,
-                                              uint32_t rank, volatile int* abort_flag) {
+                                              const Sched& sc, uint32_t rank, volatile int* abort_flag) {
   constexpr bool TMA_IN = is_update<MODE>();
   uint32_t in_phase = 0;
   LastIo io;
@@ -602,9 +701,20 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   const int quad = warp & 3;
   const int half = (warp - 2) >> 2;
   const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
-  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
-  int lt = 0;
-  for (int t = cid; t < args.n_tiles; t += ncl, ++lt) {
+  for (int lt = 0;; ++lt) {
+    // Lane 0 takes the tile for the warp (warp-uniform from here on).
+    int t = -1, got = 0;
+    if (lane == 0) {
+      got = sched_take(args, sc, lt, DEV_ERR_MBAR_TIMEOUT_EPILOGUE, &t) ? 1 : 0;
+      if (got) sched_release(sc, lt);
+    }
+    got = __shfl_sync(0xffffffffu, got, 0);
+    t = __shfl_sync(0xffffffffu, t, 0);
+    if (!got) {
+      *abort_flag = 1;
+      break;
+    }
+    if (t < 0) break;
     const TileRef tr = args.tiles[t];
     const MatDesc& md = args.mats[tr.mat];
     const int acc_buf = lt & 1;
@@ -697,8 +807,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint64_t* epi_in = drain + 1;          // one per epilogue warp: TMA fills of its X block
   uint64_t* epi_p = epi_in + EPI_WARPS;  // one per epilogue warp: TMA fills of its parameter block (UPDATE_LAST)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_p + EPI_WARPS);
+  Sched sc;
+  sc.full = epi_p + EPI_WARPS;
+  sc.empty = sc.full + SCHED_DEPTH;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc.empty + SCHED_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  sc.slot = reinterpret_cast<int32_t*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -716,6 +830,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&epi_in[w], 1);
       mbar_init(&epi_p[w], 1);
     }
+    for (int e = 0; e < SCHED_DEPTH; ++e) {
+      mbar_init(&sc.full[e], 1);
+      mbar_init(&sc.empty[e], SCHED_READERS);
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -729,13 +847,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) producer_loop<MODE>(args, ring, full, empty, rank, abort_flag);
+    if (lane == 0) producer_loop<MODE>(args, ring, full, empty, sc, rank, abort_flag);
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, abort_flag);
+    if (lane == 0 && rank == 0)
+      mma_loop<MODE>(args, ring, full, empty, tfull, tempty, drain, tmem_base, sc, abort_flag);
   } else {
     epilogue_loop<MODE>(args, tfull, tempty, tmem_base, stage_out + (warp - 2) * Smem<MODE>::STAGE_OUT,
-                        &epi_in[warp - 2], &epi_p[warp - 2],
-                        rank, abort_flag);
+                        &epi_in[warp - 2], &epi_p[warp - 2], sc, rank, abort_flag);
   }
   __syncthreads();
   if (*abort_flag && threadIdx.x == 0) {
@@ -816,6 +934,10 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
   args.lr_wd = lr_wd;
   args.lr = lr;
   args.status = status;
+  // The status word is the first field of the plan header; the scheduler's counters follow it.
+  static_assert(offsetof(PlanHeader, sched_next) == 8 && offsetof(PlanHeader, sched_retired) == 12,
+                "PlanHeader scheduler fields");
+  args.sched = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(status) + offsetof(PlanHeader, sched_next));
   args.wait_limit = MBAR_WAIT_LIMIT_CYCLES;
   args.idle_producer = 0;
   if (mode == ns::GRAM && ns::g_expire_gram_launches.load(std::memory_order_relaxed) > 0 &&

@@ -90,7 +90,12 @@ struct TileRef {
 struct PlanHeader {
   uint32_t status;   // device error bits, sticky until the host clears them
   int32_t n_mats;
-  int32_t pad[62];
+  // Tile scheduler of the Newton-Schulz GEMM launches: the next tile to hand
+  // out and the CTA pairs that have finished taking tiles.  Zero between
+  // launches (the last pair of each launch resets both).
+  int32_t sched_next;
+  int32_t sched_retired;
+  int32_t pad[60];
 };
 static_assert(sizeof(PlanHeader) == 256, "PlanHeader size");
 

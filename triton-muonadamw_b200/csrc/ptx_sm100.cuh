@@ -74,6 +74,40 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// mbar_wait with acquire at cluster scope: for a barrier that a thread of the
+// other CTA of the pair arrives on (release.cluster) after writing data into
+// this CTA's shared memory that the waiter then reads.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                                  unsigned int err_bit, long long limit = MBAR_WAIT_LIMIT_CYCLES) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    if (clock64() - t0 > limit) {
+      atomicOr(err, err_bit);
+      return false;
+    }
+  }
+}
+
+// 32-bit store to shared memory of either CTA of the cluster (a mapa address).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, int32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
