@@ -259,8 +259,9 @@ def main():
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="at N=1, skip timing the reference's own Triton MuonAdamW on this GPU after our arm")
-    ap.add_argument("--reserve-sms", type=int, default=0,
-                    help="at N>1, SMs the Newton-Schulz GEMMs leave free for the exchange (MuonAdamW reserve_sms)")
+    ap.add_argument("--reserve-sms", type=int, default=None,
+                    help="at N>1 with the NCCL exchange, SMs handed to it: the Newton-Schulz GEMMs leave them free "
+                         "and NCCL is capped to as many CTAs (MuonAdamW reserve_sms; default: the library's choice)")
     ap.add_argument("--realloc-grads", action="store_true",
                     help="alternate every step between two sets of gradient tensors (new .grad addresses each "
                          "step, as zero_grad(set_to_none=True) + backward gives): the plans patch the addresses")
@@ -315,6 +316,7 @@ def main():
     opt = MuonAdamW(model, muon_config=mcfg, adam_config=acfg, parameter_split="auto", process_group=pg,
                     peer_push=args.push, reserve_sms=args.reserve_sms)
     push_mode = opt.distributed.backend.push if opt.distributed is not None else None   # "auto" resolved
+    reserve_sms = opt.distributed.backend.reserve_sms if opt.distributed is not None else 0
     n_muon, n_adam = len(opt.muon.model_params), len(opt.adamw.model_params)
 
     def barrier():
@@ -461,12 +463,16 @@ def main():
                        "adamw_tensors": n_adam, "ns_steps": args.ns_steps, "coeffs": list(COEFFS),
                        "parallelism": "single-gpu" if world == 1 else f"muon-owner+zero1-adamw x{world}",
                        "param_push": push_mode, "realloc_grads": bool(args.realloc_grads),
-                       "reserve_sms": args.reserve_sms,
+                       "reserve_sms": reserve_sms,
                        "l2": "inputs (fp32 grads/params/momentum, > 100 GB) exceed L2; no flush needed",
                        "elementwise_dtype": "fp32"},
             "roofline": roofline, "kernels": kernels, "e2e": e2e, "gpu_launches": int(round(launches_per_step * args.steps)),
             "clocks": clock_info, "cpu_baseline": cpu,
         }
+        if clock_info.get("sm_mhz"):
+            # Under the 1 kW cap the sampled SM clock differs from box to box; time x clock
+            # compares runs (and N) per clock cycle.
+            line["ms_x_sm_ghz"] = round(ms * clock_info["sm_mhz"] / 1000.0, 1)
         if grad_reduce is not None:
             line["grad_reduce"] = grad_reduce
         if parity is not None:

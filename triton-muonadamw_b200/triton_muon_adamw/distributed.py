@@ -169,18 +169,50 @@ def _rehome(params, flat: torch.Tensor, offsets) -> None:
 
 
 # --------------------------------------------------------------------------- backends
+# NCCL communicators for the parameter exchange with a CTA cap, one per
+# (default group, ranks, cap) in this process: every optimizer over the same
+# ranks shares it instead of creating another communicator (and another set of
+# NVLS buffers).
+_EXCHANGE_GROUPS: dict = {}
+
+
+def nccl_exchange_group(process_group, ctas: int):
+    """A process group over ``process_group``'s ranks whose NCCL communicator uses at most
+    ``ctas`` CTAs per collective (NCCL config ``maxCTAs`` and ``nvlsCTAs``).
+
+    Created by every member (``use_local_synchronization``), the first time a
+    given (ranks, cap) is asked for, so the ranks must ask in the same order --
+    which constructing the optimizer collectively gives.
+    """
+    ranks = tuple(dist.get_process_group_ranks(process_group))
+    key = (id(dist.distributed_c10d._get_default_group()), ranks, int(ctas))
+    g = _EXCHANGE_GROUPS.get(key)
+    if g is None:
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.config.max_ctas = int(ctas)
+        opts.config.nvls_ctas = int(ctas)
+        g = dist.new_group(list(ranks), backend="nccl", pg_options=opts, use_local_synchronization=True)
+        _EXCHANGE_GROUPS[key] = g
+    return g
+
+
 class CudaBackend:
     """The product's arithmetic: the CUDA AdamW and Muon kernels, and the peer transfers."""
 
     PUSH_MODES = ("auto", "nccl", "copy_engine", "kernel", "hybrid")
+    # SMs handed to the NCCL exchange when "auto" picks it (more than 4 ranks):
+    # the GEMMs leave them free and the exchange communicator is capped to as
+    # many CTAs.
+    AUTO_NCCL_SMS = 8
 
-    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms: int = 0):
+    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms=None):
         if push not in self.PUSH_MODES:
             raise ValueError(f"push must be one of {self.PUSH_MODES}, got {push!r}")
-        if not 0 <= int(reserve_sms) <= 64:
-            raise ValueError(f"reserve_sms must be in 0..64, got {reserve_sms!r}")
+        if reserve_sms is not None and not 0 <= int(reserve_sms) <= 64:
+            raise ValueError(f"reserve_sms must be None or in 0..64, got {reserve_sms!r}")
         self.push = push
-        self.reserve_sms = int(reserve_sms)
+        # None: decided with the exchange (param_arena): AUTO_NCCL_SMS for NCCL, else 0.
+        self.reserve_sms = None if reserve_sms is None else int(reserve_sms)
         self.ce_splits = max(1, int(ce_splits))
         self.ce_fraction = float(ce_fraction)
         self.adam_table = AdamWTable()
@@ -203,10 +235,20 @@ class CudaBackend:
         """
         if self.push == "auto":
             self.push = "copy_engine" if dist.get_world_size(process_group) <= 4 else "nccl"
+        if self.reserve_sms is None:
+            self.reserve_sms = self.AUTO_NCCL_SMS if self.push == "nccl" else 0
         if self.push == "nccl":
             return None
         from .peer import PeerArena  # noqa: PLC0415
         return PeerArena(nbytes, device, process_group)
+
+    def exchange_group(self, process_group):
+        """The group the NCCL all-gathers of the exchange run on: with SMs
+        reserved for it, a communicator capped to that many CTAs, so NCCL's
+        kernels fit on the SMs the GEMMs leave free; else ``process_group``."""
+        if self.push != "nccl" or not self.reserve_sms:
+            return process_group
+        return nccl_exchange_group(process_group, self.reserve_sms)
 
     def push_segment(self, arena, flat: torch.Tensor, seg: int, rank: int):
         """Write this rank's segment of ``flat`` into every other rank's replica, after the work queued so
@@ -280,7 +322,7 @@ class CudaBackend:
         plan = self.plans.setdefault(bucket, MuonPlan())
         plan.ensure(triples, adjust_lr_fn, triples[0][0].device)
         run_muon_plan(plan, beta=beta, nesterov=nesterov, a=a, b=b, c=c, ns_steps=ns_steps, eps=eps, lr=lr,
-                      weight_decay=weight_decay, timer=timer, reduce=reduce, reserve_sms=self.reserve_sms)
+                      weight_decay=weight_decay, timer=timer, reduce=reduce, reserve_sms=self.reserve_sms or 0)
 
     def status(self) -> int:
         st = 0
@@ -369,6 +411,9 @@ class ShardedMuonAdamW:
         nbytes, adam_bytes, bucket_base = self._flat_layout(total)
         if hasattr(self.backend, "param_arena"):
             self.param_arena = self.backend.param_arena(nbytes, self.device, self.pg)
+        self.exchange_pg = self.pg
+        if self.param_arena is None and hasattr(self.backend, "exchange_group"):
+            self.exchange_pg = self.backend.exchange_group(self.pg)
         if self.param_arena is not None:
             raw = self.param_arena.tensor
             es = self._elem_size()
@@ -506,7 +551,7 @@ class ShardedMuonAdamW:
         if self.param_arena is not None:
             return self.backend.push_segment(self.param_arena, flat, seg, self.rank)
         mine = flat[self.rank * seg:(self.rank + 1) * seg]
-        return dist.all_gather_into_tensor(flat, mine, group=self.pg, async_op=True)
+        return dist.all_gather_into_tensor(flat, mine, group=self.exchange_pg, async_op=True)
 
     @torch.no_grad()
     def step(self, wait_for=None, adam_last=False):

@@ -172,10 +172,13 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         masters of what it owns and the all-gather moves bf16 (half the bytes).
         Checkpoints carry the masters (``"master_param"`` per parameter).
     reserve_sms:
-        With more than one rank, SMs the Newton-Schulz GEMMs leave free (0..64,
-        rounded up to pairs) so that the parameter exchange's kernels (NCCL's
-        all-gather) run beside them instead of waiting for -- and delaying --
-        a GEMM launch.  0 (default): the GEMMs use every SM.
+        With more than one rank and the NCCL exchange, SMs handed to it
+        (0..64): the Newton-Schulz GEMMs leave that many SMs free (rounded up
+        to CTA pairs) and the all-gathers run on a communicator capped to as
+        many CTAs, so NCCL's kernels run beside the GEMMs instead of waiting
+        for -- and delaying -- a GEMM launch.  None (default): 8 with the NCCL
+        exchange, 0 with the others (which use no SM, or fit beside a GEMM
+        CTA); 0 uses every SM and NCCL's own CTA count.
     """
 
     def __init__(
@@ -188,7 +191,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         reduce_grads: Literal["mean", "sum"] | None = None,
         peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid"] = "auto",
         master_weights: bool = False,
-        reserve_sms: int = 0,
+        reserve_sms: int | None = None,
     ) -> None:
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
