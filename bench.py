@@ -259,9 +259,9 @@ def main():
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="at N=1, skip timing the reference's own Triton MuonAdamW on this GPU after our arm")
-    ap.add_argument("--reserve-sms", type=int, default=None,
+    ap.add_argument("--reserve-sms", type=int, default=0,
                     help="at N>1 with the NCCL exchange, SMs handed to it: the Newton-Schulz GEMMs leave them free "
-                         "and NCCL is capped to as many CTAs (MuonAdamW reserve_sms; default: the library's choice)")
+                         "and NCCL is capped to as many CTAs (MuonAdamW reserve_sms)")
     ap.add_argument("--realloc-grads", action="store_true",
                     help="alternate every step between two sets of gradient tensors (new .grad addresses each "
                          "step, as zero_grad(set_to_none=True) + backward gives): the plans patch the addresses")

@@ -229,7 +229,7 @@ int mad_muon_step_multi_reduce(const mad_muon_plan_info* info, void* dev_table, 
  * otherwise).  Same arguments and results as planning the one matrix with
  * mad_muon_plan and calling mad_muon_step_multi; lr_scale as in
  * mad_muon_matrix.  The first call on a device resolves the array's address
- * for that device, so make it before any stream capture.  Each call uploads
+ * for that device.  Each call uploads
  * its plan synchronously and, once its kernels have finished, reads their
  * status word back: MAD_ERR_DEVICE if one gave up waiting on a barrier (the
  * parameter and momentum it wrote are then invalid).  Calls that overlap on

@@ -388,21 +388,16 @@ def test_cuda_backend_offers_every_call_the_sharded_step_makes():
         CudaBackend(push="tree")
 
 
-def test_sms_handed_to_the_nccl_exchange_default_and_override():
-    """reserve_sms=None resolves with the exchange: 8 SMs for NCCL (GEMMs leave them free, the
-    exchange communicator is capped to 8 CTAs), 0 for the exchanges that need no SM beside the
-    GEMMs; an explicit 0 keeps the caller's group and NCCL's own CTA count."""
+def test_sms_handed_to_the_nccl_exchange():
+    """reserve_sms=0 (default) keeps the caller's group for the NCCL all-gathers (NCCL's own CTA
+    count, every SM for the GEMMs); a reserve applies to the NCCL exchange only."""
     from triton_muon_adamw.distributed import CudaBackend
 
-    b = CudaBackend(push="nccl")
-    assert b.reserve_sms is None
-    assert b.param_arena(1 << 20, torch.device("cpu"), None) is None
-    assert b.reserve_sms == CudaBackend.AUTO_NCCL_SMS == 8
-    plain = CudaBackend(push="nccl", reserve_sms=0)
-    plain.param_arena(1 << 20, torch.device("cpu"), None)
     sentinel = object()
-    assert plain.exchange_group(sentinel) is sentinel
-    ce = CudaBackend(push="copy_engine")
-    assert ce.exchange_group(sentinel) is sentinel
+    b = CudaBackend(push="nccl")
+    assert b.reserve_sms == 0
+    assert b.param_arena(1 << 20, torch.device("cpu"), None) is None
+    assert b.exchange_group(sentinel) is sentinel
+    assert CudaBackend(push="copy_engine", reserve_sms=8).exchange_group(sentinel) is sentinel
     with pytest.raises(ValueError):
         CudaBackend(push="nccl", reserve_sms=65)

@@ -17,12 +17,11 @@
 // call rewrites the whole plan (counters and status start at zero).  Calls
 // that overlap on the GPU (different streams, or different host threads
 // without ordering) race on it.  The first call on a device resolves the
-// array's device address for that device (cudaGetSymbolAddress), so make the
-// first call before any stream capture.  Each call uploads its plan with a
-// synchronous copy, which also waits for the stream's earlier work, and after
-// its kernels reads their status word back (waiting for them to finish): a
-// kernel that gave up waiting on a barrier makes the call return
-// MAD_ERR_DEVICE.
+// array's device address for that device (cudaGetSymbolAddress).  Each call
+// uploads its plan with a synchronous copy, which also waits for the stream's
+// earlier work, and after its kernels reads their status word back (waiting
+// for them to finish): a kernel that gave up waiting on a barrier makes the
+// call return MAD_ERR_DEVICE.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>

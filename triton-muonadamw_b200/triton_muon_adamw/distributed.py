@@ -200,19 +200,20 @@ class CudaBackend:
     """The product's arithmetic: the CUDA AdamW and Muon kernels, and the peer transfers."""
 
     PUSH_MODES = ("auto", "nccl", "copy_engine", "kernel", "hybrid")
-    # SMs handed to the NCCL exchange when "auto" picks it (more than 4 ranks):
-    # the GEMMs leave them free and the exchange communicator is capped to as
-    # many CTAs.
-    AUTO_NCCL_SMS = 8
 
-    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms=None):
+    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms: int = 0):
         if push not in self.PUSH_MODES:
             raise ValueError(f"push must be one of {self.PUSH_MODES}, got {push!r}")
-        if reserve_sms is not None and not 0 <= int(reserve_sms) <= 64:
-            raise ValueError(f"reserve_sms must be None or in 0..64, got {reserve_sms!r}")
+        if not 0 <= int(reserve_sms) <= 64:
+            raise ValueError(f"reserve_sms must be in 0..64, got {reserve_sms!r}")
         self.push = push
-        # None: decided with the exchange (param_arena): AUTO_NCCL_SMS for NCCL, else 0.
-        self.reserve_sms = None if reserve_sms is None else int(reserve_sms)
+        # SMs handed to the NCCL exchange: the GEMMs leave them free and the
+        # exchange communicator is capped to as many CTAs.  0 (default): every
+        # SM for the GEMMs, NCCL's own CTA count.  Measured on the 8B step at
+        # 4 ranks, a cap of 8 CTAs kept the GEMMs at their single-rank rate
+        # per clock but left the all-gather too slow to hide (197 ms/step
+        # against 125 without a cap; 16: 136 ms).
+        self.reserve_sms = int(reserve_sms)
         self.ce_splits = max(1, int(ce_splits))
         self.ce_fraction = float(ce_fraction)
         self.adam_table = AdamWTable()
@@ -235,8 +236,6 @@ class CudaBackend:
         """
         if self.push == "auto":
             self.push = "copy_engine" if dist.get_world_size(process_group) <= 4 else "nccl"
-        if self.reserve_sms is None:
-            self.reserve_sms = self.AUTO_NCCL_SMS if self.push == "nccl" else 0
         if self.push == "nccl":
             return None
         from .peer import PeerArena  # noqa: PLC0415
@@ -322,7 +321,7 @@ class CudaBackend:
         plan = self.plans.setdefault(bucket, MuonPlan())
         plan.ensure(triples, adjust_lr_fn, triples[0][0].device)
         run_muon_plan(plan, beta=beta, nesterov=nesterov, a=a, b=b, c=c, ns_steps=ns_steps, eps=eps, lr=lr,
-                      weight_decay=weight_decay, timer=timer, reduce=reduce, reserve_sms=self.reserve_sms or 0)
+                      weight_decay=weight_decay, timer=timer, reduce=reduce, reserve_sms=self.reserve_sms)
 
     def status(self) -> int:
         st = 0

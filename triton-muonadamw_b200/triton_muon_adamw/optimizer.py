@@ -175,10 +175,11 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         With more than one rank and the NCCL exchange, SMs handed to it
         (0..64): the Newton-Schulz GEMMs leave that many SMs free (rounded up
         to CTA pairs) and the all-gathers run on a communicator capped to as
-        many CTAs, so NCCL's kernels run beside the GEMMs instead of waiting
-        for -- and delaying -- a GEMM launch.  None (default): 8 with the NCCL
-        exchange, 0 with the others (which use no SM, or fit beside a GEMM
-        CTA); 0 uses every SM and NCCL's own CTA count.
+        many CTAs, so NCCL's kernels run beside the GEMMs instead of taking
+        SMs from them.  0 (default): every SM for the GEMMs and NCCL's own CTA
+        count -- the faster choice measured (the GEMMs hand out tiles
+        dynamically, so a pair whose SMs NCCL holds for a while takes fewer
+        tiles, while a capped all-gather falls behind the compute).
     """
 
     def __init__(
@@ -191,7 +192,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         reduce_grads: Literal["mean", "sum"] | None = None,
         peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid"] = "auto",
         master_weights: bool = False,
-        reserve_sms: int | None = None,
+        reserve_sms: int = 0,
     ) -> None:
         if reduce_grads not in (None, "mean", "sum"):
             raise ValueError(f"reduce_grads must be None, 'mean' or 'sum', got {reduce_grads!r}")
