@@ -556,14 +556,32 @@ def run_e2e(opt, model, dev, args, barrier, world):
     end.record()
     barrier()
     ms = start.elapsed_time(end) / steps
+    # What the host link gives one plain copy: 1 GiB of the same pinned buffer to the device,
+    # on every rank at once (the ranks share the host's memory and PCIe switches).
+    n = min(flat.numel(), (1 << 30) // 4)
+    dst = torch.empty(n, dtype=torch.float32, device=dev)
+    dst.copy_(flat[:n], non_blocking=True)
+    barrier()
+    start.record()
+    for _ in range(3):
+        dst.copy_(flat[:n], non_blocking=True)
+    end.record()
+    barrier()
+    copy_gbs = 3 * n * 4 / (start.elapsed_time(end) * 1e-3) / 1e9
+    del dst
     if world > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, -copy_gbs], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, copy_gbs = float(t[0].item()), -float(t[1].item())
     return {"value": round(ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(out.numel() * 4), "steps": steps,
+            "h2d_gbs": round(h2d / (ms * 1e-3) / 1e9, 1),
+            "h2d_copy_gbs": round(copy_gbs, 1),
+            "h2d_bound_ms": round(h2d / (copy_gbs * 1e9) * 1e3, 1),
             "what": "MuonAdamW.step_from_host (grads H2D from pinned memory, overlapped) + final-norm D2H, "
-                    "device-timed"}
+                    "device-timed; h2d_gbs = this rank's gradient bytes / step time, h2d_copy_gbs = a plain "
+                    "1 GiB pinned copy on every rank at once (slowest rank), h2d_bound_ms = the step's "
+                    "gradient bytes at that rate"}
 
 
 def run_grad_reduce(model, mcfg, acfg, args, dev, pg, world, rank, barrier):
