@@ -177,7 +177,7 @@ extern "C" int mad_muon_step_noalloc(float* param, const float* grad, float* mom
   // Tile lists in the planner's order: 256x256 tiles, column-block-major; Gram and
   // polynomial only on or above the diagonal.
   const int64_t tms = (m + 255) / 256, tns_x = (n + 255) / 256;
-  auto emit = [&](int64_t off, bool triangle) {
+  auto emit = [&](int64_t off, bool triangle, int64_t k_extent) {
     TileRef* out = reinterpret_cast<TileRef*>(g_host_image + off);
     int64_t k = 0;
     for (int64_t tn = 0; tn < (triangle ? tms : tns_x); ++tn)
@@ -185,13 +185,13 @@ extern "C" int mad_muon_step_noalloc(float* param, const float* grad, float* mom
         out[k].mat = 0;
         out[k].tm = static_cast<int32_t>(tm);
         out[k].tn = static_cast<int32_t>(tn);
-        out[k].pad = 0;
+        out[k].nkb = static_cast<int32_t>((k_extent + 63) / 64);
         ++k;
       }
     return k;
   };
-  if (emit(info.off_gram_tiles, true) != info.gram_tiles || emit(info.off_poly_tiles, true) != info.poly_tiles ||
-      emit(info.off_update_tiles, false) != info.update_tiles)
+  if (emit(info.off_gram_tiles, true, n) != info.gram_tiles || emit(info.off_poly_tiles, true, m) != info.poly_tiles ||
+      emit(info.off_update_tiles, false, m) != info.update_tiles)
     return fail(MAD_ERR_INVALID, "mad_muon_step_noalloc: internal tile count mismatch");
   // prep tile -> matrix map is all zeros (one matrix); partial sums are written before they are read.
 

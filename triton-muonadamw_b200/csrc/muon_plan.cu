@@ -30,7 +30,7 @@ int launch_ns_gemm(int mode, const MatDesc* mats, const CUtensorMap* tmaps, cons
 namespace {
 
 // Output tiles are computed by CTA pairs: 256 x 256 (each CTA 128 rows).
-constexpr int GEMM_BM = 256, GEMM_BN = 256;
+constexpr int GEMM_BM = 256, GEMM_BN = 256, GEMM_BK = 64;
 
 inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -305,7 +305,7 @@ extern "C" int mad_muon_plan(const mad_muon_matrix* mats, int32_t n_mats, void* 
           out[k].mat = i;
           out[k].tm = static_cast<int32_t>(tmi);
           out[k].tn = static_cast<int32_t>(tn);
-          out[k].pad = 0;
+          out[k].nkb = static_cast<int32_t>(((gram_k ? s.n : s.m) + GEMM_BK - 1) / GEMM_BK);
           ++k;
         }
       }

@@ -99,34 +99,44 @@ struct GemmArgs {
   int idle_producer;     // test launches only: the producer issues no loads, so the waits expire
 };
 
-__device__ __forceinline__ int k_extent(int mode, const MatDesc& md) { return mode == GRAM ? md.n : md.m; }
 
 // ---------------------------------------------------------------- tile scheduler
 // Ring of tile indices, one copy in each CTA of the pair.  Entry j is written
-// by the leader's producer (a tile index, or -1 when none is left) and read by
-// every other role of the pair: the leader's MMA thread and epilogue warps,
-// the peer's producer and epilogue warps.  Each reader arrives on the leader's
-// `empty` barrier of the entry; the producer reuses it after all of them.
+// by the leader's producer (a tile index, or -1 when none is left, and the
+// tile's K-block count) and read by every other role of the pair: the leader's
+// MMA thread and epilogue warps, the peer's producer and epilogue warps.  Each
+// reader arrives on the leader's `empty` barrier of the entry; the producer
+// reuses it after all of them.  The MMA thread needs nothing else of a tile,
+// so it issues the next tile's MMAs without a global-memory round trip.
 constexpr int SCHED_DEPTH = 8;
 constexpr uint32_t SCHED_READERS = 1 + EPI_WARPS + 1 + EPI_WARPS;
 
 struct Sched {
-  int32_t* slot;     // [SCHED_DEPTH]
+  int32_t* slot;     // [SCHED_DEPTH] tile index
+  int32_t* kblk;     // [SCHED_DEPTH] its TileRef::nkb
   uint64_t* full;    // [SCHED_DEPTH], one arrival (the leader's producer)
   uint64_t* empty;   // [SCHED_DEPTH], SCHED_READERS arrivals; only the leader's are used
 };
 
-// Leader producer: takes the next tile and publishes it as entry j.  False if
-// the entry's previous readers did not release it in time.
-__device__ __forceinline__ bool sched_publish(const GemmArgs& args, const Sched& sc, int j, int* tile) {
+// Leader producer: takes the next tile, reads its TileRef and publishes both as
+// entry j.  False if the entry's previous readers did not release it in time.
+__device__ __forceinline__ bool sched_publish(const GemmArgs& args, const Sched& sc, int j, int* tile, TileRef* tr) {
   const int s = j % SCHED_DEPTH;
   const uint32_t ph = static_cast<uint32_t>((j / SCHED_DEPTH) & 1);
   if (!mbar_wait_cluster(&sc.empty[s], ph ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_PRODUCER, args.wait_limit))
     return false;
   int t = atomicAdd(&args.sched[0], 1);
-  if (t >= args.n_tiles) t = -1;
+  int nkb = 0;
+  if (t >= args.n_tiles) {
+    t = -1;
+  } else {
+    *tr = args.tiles[t];
+    nkb = tr->nkb;
+  }
   sc.slot[s] = t;
+  sc.kblk[s] = nkb;
   st_shared_cluster_u32(mapa_shared(smem_u32(&sc.slot[s]), 1), t);
+  st_shared_cluster_u32(mapa_shared(smem_u32(&sc.kblk[s]), 1), nkb);
   mbar_arrive(&sc.full[s]);
   mbar_arrive_cluster(mapa_shared(smem_u32(&sc.full[s]), 1));
   *tile = t;
@@ -136,11 +146,12 @@ __device__ __forceinline__ bool sched_publish(const GemmArgs& args, const Sched&
 // Any other role: waits for entry j and reads it (every lane of a warp may
 // call this; `release` then runs on one lane after the warp has read it).
 __device__ __forceinline__ bool sched_take(const GemmArgs& args, const Sched& sc, int j, unsigned int err_bit,
-                                           int* tile) {
+                                           int* tile, int* nkb = nullptr) {
   const int s = j % SCHED_DEPTH;
   const uint32_t ph = static_cast<uint32_t>((j / SCHED_DEPTH) & 1);
   if (!mbar_wait_cluster(&sc.full[s], ph, args.status, err_bit, args.wait_limit)) return false;
   *tile = *reinterpret_cast<volatile int32_t*>(&sc.slot[s]);
+  if (nkb) *nkb = *reinterpret_cast<volatile int32_t*>(&sc.kblk[s]);
   return true;
 }
 
@@ -175,17 +186,20 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
     // Test launches: one tile is handed out and nothing is loaded, so the
     // MMA and epilogue waits of that tile expire.
     int t;
+    TileRef tr;
     if (rank == 0) {
-      sched_publish(args, sc, 0, &t);
+      sched_publish(args, sc, 0, &t, &tr);
       sched_retire(args);
     }
     return;
   }
   bool ok = true;
+  int acquired = -1;  // matrix whose tensor maps this thread has acquired
   for (int j = 0; ok; ++j) {
     int t;
+    TileRef tr;
     if (rank == 0) {
-      if (!sched_publish(args, sc, j, &t)) {
+      if (!sched_publish(args, sc, j, &t, &tr)) {
         *abort_flag = 1;
         break;
       }
@@ -195,11 +209,10 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
         break;
       }
       sched_release(sc, j);
+      if (t >= 0) tr = args.tiles[t];
     }
     if (t < 0) break;
-    const TileRef tr = args.tiles[t];
-    const MatDesc& md = args.mats[tr.mat];
-    const CUtensorMap* maps = args.tmaps + md.tmap_base;
+    const CUtensorMap* maps = args.tmaps + tr.mat * TMAPS_PER_MAT;
     const CUtensorMap* tmA;
     const CUtensorMap* tmB;
     if (MODE == GRAM) {
@@ -210,11 +223,14 @@ __device__ __forceinline__ void producer_loop(const GemmArgs& args, uint8_t* rin
       tmA = maps + TM_POLY;
       tmB = maps + (TM_XMN0 + cur);
     }
-    tma_acquire_desc(tmA);
-    if (tmB != tmA) tma_acquire_desc(tmB);
+    if (tr.mat != acquired) {  // once per matrix: later uses by this thread are ordered after it
+      tma_acquire_desc(tmA);
+      if (tmB != tmA) tma_acquire_desc(tmB);
+      acquired = tr.mat;
+    }
     const int arow = tr.tm * PAIR_M + static_cast<int>(rank) * BM;     // this CTA's A rows
     const int bcol = tr.tn * BN + static_cast<int>(rank) * (BN / 2);   // this CTA's B columns
-    const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
+    const int nkb = tr.nkb;
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_PRODUCER, args.wait_limit) ||
           *abort_flag) {
@@ -254,16 +270,13 @@ __device__ __forceinline__ void mma_loop(const GemmArgs& args, uint8_t* ring, ui
   uint32_t phase = 0;
   bool ok = true;
   for (int lt = 0; ok; ++lt) {
-    int t;
-    if (!sched_take(args, sc, lt, DEV_ERR_MBAR_TIMEOUT_MMA, &t)) {
+    int t, nkb;
+    if (!sched_take(args, sc, lt, DEV_ERR_MBAR_TIMEOUT_MMA, &t, &nkb)) {
       *abort_flag = 1;
       break;
     }
     sched_release(sc, lt);
     if (t < 0) break;
-    const TileRef tr = args.tiles[t];
-    const MatDesc& md = args.mats[tr.mat];
-    const int nkb = (k_extent(MODE, md) + BK - 1) / BK;
     const int acc = lt & 1;
     const uint32_t acc_phase = static_cast<uint32_t>((lt >> 1) & 1);
     if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.status, DEV_ERR_MBAR_TIMEOUT_MMA, args.wait_limit) ||
@@ -701,6 +714,7 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
   const int quad = warp & 3;
   const int half = (warp - 2) >> 2;
   const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
+  int acquired = -1, acquired_p = -1;  // matrices whose store/input and parameter maps lane 0 has acquired
   for (int lt = 0;; ++lt) {
     // Lane 0 takes the tile for the warp (warp-uniform from here on).
     int t = -1, got = 0;
@@ -734,17 +748,21 @@ __device__ __forceinline__ void epilogue_loop(const GemmArgs& args, uint64_t* tf
     const bool warp_rows = grow0 < md.m;  // some of this warp's rows exist (warp-uniform)
     const CUtensorMap* in_map = args.tmaps + md.tmap_base + TM_X0_ST + (args.iter & 1);
 
-    if (lane == 0 && MODE != UPDATE_LAST) {
-      const int st = MODE == GRAM ? TM_GRAM_ST : MODE == POLY ? TM_POLY_ST : TM_X0_ST + ((args.iter & 1) ^ 1);
-      tma_acquire_desc(args.tmaps + md.tmap_base + st);
+    if (lane == 0 && tr.mat != acquired) {  // once per matrix: later uses by this thread are ordered after it
+      if (MODE != UPDATE_LAST) {
+        const int st = MODE == GRAM ? TM_GRAM_ST : MODE == POLY ? TM_POLY_ST : TM_X0_ST + ((args.iter & 1) ^ 1);
+        tma_acquire_desc(args.tmaps + md.tmap_base + st);
+      }
+      if (TMA_IN) tma_acquire_desc(in_map);
+      acquired = tr.mat;
     }
-    if (lane == 0 && TMA_IN) tma_acquire_desc(in_map);
     io.on = (MODE == UPDATE_LAST && md.p_tma && warp_rows && nch > 0) ? 1u : 0u;
     if (io.on) {
       const CUtensorMap* maps = args.tmaps + md.tmap_base;
-      if (lane == 0) {
+      if (lane == 0 && tr.mat != acquired_p) {
         tma_acquire_desc(maps + TM_P);
         if (md.dtype == MAD_DTYPE_F32_MASTER) tma_acquire_desc(maps + TM_SH);
+        acquired_p = tr.mat;
       }
       last_p_issue(md, maps, stage, io, grow0, col0);  // chunk 0's block arrives while the accumulator completes
     }
@@ -813,6 +831,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc.empty + SCHED_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   sc.slot = reinterpret_cast<int32_t*>(tmem_slot + 2);
+  sc.kblk = sc.slot + SCHED_DEPTH;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();

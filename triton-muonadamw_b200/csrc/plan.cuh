@@ -80,11 +80,14 @@ struct MatDesc {
 };
 static_assert(sizeof(MatDesc) == 136, "MatDesc layout");
 
+// One 256x256 output tile of a Newton-Schulz product.  The tile lists are
+// built with MatDesc::tmap_base == mat * TMAPS_PER_MAT, so a kernel can find a
+// tile's tensor maps without reading its MatDesc.
 struct TileRef {
   int32_t mat;
-  int32_t tm;  // row block (128 rows)
-  int32_t tn;  // column block (256 columns)
-  int32_t pad;
+  int32_t tm;   // row block (256 rows: a CTA pair's two 128-row halves)
+  int32_t tn;   // column block (256 columns)
+  int32_t nkb;  // 64-wide blocks of this product's K extent (n for X Xᵀ, m otherwise)
 };
 
 struct PlanHeader {
