@@ -253,7 +253,7 @@ def main():
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--push", default="auto", choices=["auto", "nccl", "copy_engine", "kernel", "hybrid"],
+    ap.add_argument("--push", default="auto", choices=["auto", "nccl", "copy_engine", "kernel", "hybrid", "mixed"],
                     help="at N>1, how updated parameters reach the other ranks (MuonAdamW peer_push)")
     ap.add_argument("--no-grad-reduce", action="store_true",
                     help="at N>1, skip timing the step with per-rank gradients reduced inside it (reduce_grads)")

@@ -401,3 +401,20 @@ def test_sms_handed_to_the_nccl_exchange():
     assert CudaBackend(push="copy_engine", reserve_sms=8).exchange_group(sentinel) is sentinel
     with pytest.raises(ValueError):
         CudaBackend(push="nccl", reserve_sms=65)
+
+
+def test_mixed_exchange_sends_the_early_exchanges_by_copy_engine():
+    """push="mixed": the first ce_exchanges exchanges of a step are written into the peers'
+    replicas (copy engines), the later ones go by NCCL all-gather; the other modes are uniform."""
+    from triton_muon_adamw.distributed import CudaBackend
+
+    b = CudaBackend(push="mixed")
+    assert [b.exchange_kind(i) for i in range(6)] == ["push"] * 3 + ["nccl"] * 3
+    b = CudaBackend(push="mixed", ce_exchanges=1)
+    assert [b.exchange_kind(i) for i in range(3)] == ["push", "nccl", "nccl"]
+    assert CudaBackend(push="copy_engine").exchange_kind(9) == "push"
+    n = CudaBackend(push="nccl")
+    n.param_arena(1 << 20, torch.device("cpu"), None)
+    assert n.exchange_kind(0) == "nccl"
+    with pytest.raises(ValueError):
+        CudaBackend(push="mixed", ce_exchanges=-1)

@@ -250,8 +250,8 @@ def _spawn(target, world, *extra):
     return out
 
 
-@pytest.mark.parametrize("world,push", [(2, "auto"), (2, "nccl"), (2, "kernel"), (2, "hybrid"), (4, "auto"),
-                                        (8, "auto"), (8, "copy_engine")])
+@pytest.mark.parametrize("world,push", [(2, "auto"), (2, "nccl"), (2, "kernel"), (2, "hybrid"), (2, "mixed"),
+                                        (4, "auto"), (8, "auto"), (8, "copy_engine"), (8, "mixed")])
 def test_sharded_step_is_bit_identical(world, push):
     """Every way of exchanging the updated parameters (peer_push), at 2, 4 and 8 ranks -- 8 with the
     NCCL all-gather that "auto" picks there, as in the scaling runs -- gives the single-GPU result."""

@@ -199,14 +199,20 @@ def nccl_exchange_group(process_group, ctas: int):
 class CudaBackend:
     """The product's arithmetic: the CUDA AdamW and Muon kernels, and the peer transfers."""
 
-    PUSH_MODES = ("auto", "nccl", "copy_engine", "kernel", "hybrid")
+    PUSH_MODES = ("auto", "nccl", "copy_engine", "kernel", "hybrid", "mixed")
 
-    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms: int = 0):
+    def __init__(self, push: str = "auto", ce_splits: int = 1, ce_fraction: float = 0.5, reserve_sms: int = 0,
+                 ce_exchanges: int = 3):
         if push not in self.PUSH_MODES:
             raise ValueError(f"push must be one of {self.PUSH_MODES}, got {push!r}")
         if not 0 <= int(reserve_sms) <= 64:
             raise ValueError(f"reserve_sms must be in 0..64, got {reserve_sms!r}")
+        if int(ce_exchanges) < 0:
+            raise ValueError(f"ce_exchanges must be >= 0, got {ce_exchanges!r}")
         self.push = push
+        # push="mixed": the first ce_exchanges exchanges issued in a step go by the
+        # copy engines, the later ones by NCCL all-gathers (see exchange_kind).
+        self.ce_exchanges = int(ce_exchanges)
         # SMs handed to the NCCL exchange: the GEMMs leave them free and the
         # exchange communicator is capped to as many CTAs.  0 (default): every
         # SM for the GEMMs, NCCL's own CTA count.  Measured on the 8B step at
@@ -241,6 +247,22 @@ class CudaBackend:
         from .peer import PeerArena  # noqa: PLC0415
         return PeerArena(nbytes, device, process_group)
 
+    def exchange_kind(self, index: int) -> str:
+        """How the ``index``-th exchange issued in a step moves: ``"push"`` (written into
+        the peers' replicas, :meth:`push_segment`) or ``"nccl"`` (all-gather).
+
+        ``push="mixed"`` splits a step's exchanges: the early ones -- issued
+        while most of the step's compute is still ahead, and carrying most of
+        the bytes (the AdamW flat and the largest Muon buckets) -- go by the
+        copy engines, which use no SM; only the late ones go by NCCL, whose
+        kernels take SMs from the Newton-Schulz GEMMs while they run.
+        """
+        if self.push == "nccl":
+            return "nccl"
+        if self.push == "mixed":
+            return "push" if index < self.ce_exchanges else "nccl"
+        return "push"
+
     def exchange_group(self, process_group):
         """The group the NCCL all-gathers of the exchange run on: with SMs
         reserved for it, a communicator capped to that many CTAs, so NCCL's
@@ -261,7 +283,7 @@ class CudaBackend:
         ``push="hybrid"``: the first ``ce_fraction`` of the segment by the copy
         engines, the rest by the kernel, concurrently.
         """
-        if self.push not in ("kernel", "copy_engine", "hybrid"):
+        if self.push not in ("kernel", "copy_engine", "hybrid", "mixed"):
             raise ValueError(f"push mode {self.push!r} does not write into peer replicas")
         lib = _lib.load()
         cur = torch.cuda.current_stream()
@@ -275,7 +297,8 @@ class CudaBackend:
         off = src.data_ptr() - arena.ptr
         nbytes = src.numel() * src.element_size()
         peers = [(rank + k) % arena.world for k in range(1, arena.world)]
-        ce_bytes = {"kernel": 0, "copy_engine": nbytes}.get(self.push, int(nbytes * self.ce_fraction) // 256 * 256)
+        ce_bytes = {"kernel": 0, "copy_engine": nbytes, "mixed": nbytes}.get(
+            self.push, int(nbytes * self.ce_fraction) // 256 * 256)
         done = []
 
         def finish(st):
@@ -411,6 +434,7 @@ class ShardedMuonAdamW:
         if hasattr(self.backend, "param_arena"):
             self.param_arena = self.backend.param_arena(nbytes, self.device, self.pg)
         self.exchange_pg = self.pg
+        self._exchanges_issued = 0
         if self.param_arena is None and hasattr(self.backend, "exchange_group"):
             self.exchange_pg = self.backend.exchange_group(self.pg)
         if self.param_arena is not None:
@@ -547,7 +571,10 @@ class ShardedMuonAdamW:
 
     def _gather(self, flat: torch.Tensor, seg: int):
         """Refresh every replica of ``flat`` with this rank's segment (returns a work with ``wait()``)."""
-        if self.param_arena is not None:
+        index = self._exchanges_issued
+        self._exchanges_issued += 1
+        kind = self.backend.exchange_kind(index) if hasattr(self.backend, "exchange_kind") else "push"
+        if self.param_arena is not None and kind == "push":
             return self.backend.push_segment(self.param_arena, flat, seg, self.rank)
         mine = flat[self.rank * seg:(self.rank + 1) * seg]
         return dist.all_gather_into_tensor(flat, mine, group=self.exchange_pg, async_op=True)
@@ -561,6 +588,7 @@ class ShardedMuonAdamW:
         ad, mu = self.adamw, self.muon
         ad.step_num += 1
         works = []
+        self._exchanges_issued = 0
         bias1, bias2 = 1 - ad.beta1 ** ad.step_num, 1 - ad.beta2 ** ad.step_num
         red = None
         if getattr(self, "closed", False):

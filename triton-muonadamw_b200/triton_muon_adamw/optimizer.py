@@ -160,8 +160,10 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         others: ``"auto"`` (default; the copy engines up to 4 ranks, NCCL
         above), ``"nccl"`` (all-gather), ``"copy_engine"`` (each rank writes its
         segment into the others' replicas with ``cudaMemcpyAsync``, no SM),
-        ``"kernel"`` (a small broadcast kernel beside the GEMMs) or
-        ``"hybrid"`` (copy engines and kernel, half each).
+        ``"kernel"`` (a small broadcast kernel beside the GEMMs),
+        ``"hybrid"`` (copy engines and kernel, half each) or ``"mixed"`` (the
+        step's first three exchanges by the copy engines, the later ones by
+        NCCL).
     master_weights:
         Mixed precision: the parameters (and their gradients) are bfloat16 and
         the optimizer keeps a float32 master copy of each, with float32 Muon
@@ -190,7 +192,7 @@ class MuonAdamW(TritonMuon, TritonAdamW):
         parameter_split: Literal["auto", "explicit"] = "auto",
         process_group=None,
         reduce_grads: Literal["mean", "sum"] | None = None,
-        peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid"] = "auto",
+        peer_push: Literal["auto", "nccl", "copy_engine", "kernel", "hybrid", "mixed"] = "auto",
         master_weights: bool = False,
         reserve_sms: int = 0,
     ) -> None:
