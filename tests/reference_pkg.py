@@ -1,7 +1,8 @@
 """Import the unmodified reference package for side-by-side GPU tests.
 
 The reference (Mithun-033/Triton-MuonAdamW, ``MuonAdamW package/``) is
-installed unmodified under ``baseline/_ref``.  Its package
+installed unmodified under ``baseline/_ref`` (a pure-Python wheel of its
+``triton_muon_adamw/`` files, installed with ``pip --target``).  Its package
 has the same import name as ours, ``triton_muon_adamw``, so it is loaded here
 under the alias ``ref_triton_muon_adamw``; its modules use relative imports
 only, so nothing of it resolves to our package.  Test infrastructure only.
@@ -24,8 +25,8 @@ def load_reference():
     init = REF_ROOT / "triton_muon_adamw" / "__init__.py"
     if not init.exists():
         raise FileNotFoundError(
-            f"{init} is missing: install the reference into baseline/_ref (DESIGN.md, 'Reference install') "
-            "before running the reference parity tests")
+            f"{init} is missing: install the reference package into baseline/_ref "
+            "(pip install --no-deps --target baseline/_ref) before running the reference parity tests")
     spec = importlib.util.spec_from_file_location(ALIAS, init, submodule_search_locations=[str(init.parent)])
     mod = importlib.util.module_from_spec(spec)
     sys.modules[ALIAS] = mod
